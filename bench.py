@@ -1,0 +1,399 @@
+"""Benchmark: flat PQ search queries/s on B200 (BASELINE.json metric), one JSON line on stdout (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1] [--m 16] [--impl ours|reference]
+
+Default workload: config 1 (1M SIFT-shaped mixture vectors, d=128, PQ m=16, nq=1,000, k=10), the configuration
+the reference's headline number is quoted on. With N > 1 (torchrun, one process per GPU) the database is sharded
+contiguously by id: each rank searches its shard (global ids), the per-rank top-k lists are all-gathered over
+NCCL and merged on the GPU by the same warp-merge kernel (strong scaling: total work fixed).
+
+A step = one search of all nq queries: LUT build -> fused scan + top-k -> merge.
+  value  device-resident: queries already in HBM, results left in HBM; CUDA events on the launching stream,
+         L2 flushed (256 MB write) before every timed step, outside the events.
+  e2e    the reference-facing call (vk_search: host queries in pinned memory -> host results), host<->device
+         copies inside; its stage timings (CUDA events on the index's stream) give the scan kernel's duration
+         for the roofline.
+--impl reference: the reference's own CPU path (adc_search, built from its sources into oracle/_ref) timed on
+this box's host cores on a bounded query sample of the same workload; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import signal
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", default="c1")
+    p.add_argument("--m", type=int, default=None)
+    p.add_argument("--n", type=int, default=None)
+    p.add_argument("--nq", type=int, default=None)
+    p.add_argument("--k", type=int, default=None)
+    p.add_argument("--qpb", type=int, default=4, help="queries per block (Q)")
+    p.add_argument("--ilp", type=int, default=2, help="32-row groups per warp step")
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample duration")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------------------------------------ helpers
+def rank_info():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled every 200 ms during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"vk_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.send_signal(signal.SIGTERM)
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max((float(r[3]) for r in rows if r[3].replace(".", "").isdigit()), default=None)}
+
+
+def lookup_wavefront_model(codes: np.ndarray, Q: int, sample_rows: int = 1 << 17) -> float:
+    """Mean shared-memory wavefronts per warp-wide LUT fetch for these codes under the scan kernel's layout
+    ([s][c][Q] entries: LDS.32 / .64 / .128 for Q = 1 / 2 / 4 and 8; 32 consecutive rows per warp instruction):
+    per phase of 32 / 16 / 8 lanes, the max over 128-byte bank groups of distinct entries addressed."""
+    n, m = codes.shape
+    rows = min(n, sample_rows) // 32 * 32
+    c = codes[:rows].reshape(-1, 32, m).astype(np.int64)  # [warps, lanes, m]
+    lanes_per_phase = {1: 32, 2: 16, 4: 8, 8: 8}[Q]
+    entry_banks = {1: 1, 2: 2, 4: 4, 8: 4}[Q]
+    groups = 32 // entry_banks
+    total = 0.0
+    for ph in range(32 // lanes_per_phase):
+        cc = c[:, ph * lanes_per_phase:(ph + 1) * lanes_per_phase, :]  # [warps, lanes, m]
+        bank = cc % groups
+        # distinct entries per bank group: count unique codes per (warp, s, bank)
+        key = (cc * groups + bank)  # unique code implies unique key
+        w, l, s = key.shape
+        k2 = np.sort(key.transpose(0, 2, 1).reshape(-1, l), axis=1)
+        distinct = np.ones_like(k2, dtype=bool)
+        distinct[:, 1:] = k2[:, 1:] != k2[:, :-1]
+        b2 = k2 % groups
+        load = np.zeros((k2.shape[0], groups), np.int64)
+        np.add.at(load, (np.repeat(np.arange(k2.shape[0]), l), b2.ravel()), distinct.ravel())
+        total += load.max(axis=1).mean()
+    return total  # wavefronts per warp instruction (all phases)
+
+
+# ------------------------------------------------------------------------------------------------ workload
+def build_workload(args, rank: int, world: int):
+    from veckern_b200 import configs
+
+    spec = configs.spec(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k)
+    w = configs.make(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k, encode=gpu_encoder())
+    return spec, w
+
+
+def gpu_encoder():
+    """Bit-exact PQ encode on the GPU (vk_encode_device), in 1M-row slices."""
+    def enc(cent, x):
+        import torch
+
+        from veckern_b200 import _native as N
+        m, _, dsub = cent.shape
+        out = np.empty((x.shape[0], m), np.uint8)
+        dev = torch.cuda.current_device()
+        step = 1 << 20
+        for a in range(0, x.shape[0], step):
+            xs = torch.from_numpy(np.ascontiguousarray(x[a:a + step])).cuda()
+            cs = torch.empty((xs.shape[0], m), dtype=torch.uint8, device="cuda")
+            N.check(N.lib().vk_encode_device(dev, N.ptr(np.ascontiguousarray(cent)), m, dsub, N.ptr(xs),
+                                             xs.shape[0], N.ptr(cs), torch.cuda.current_stream().cuda_stream),
+                    "encode")
+            out[a:a + xs.shape[0]] = cs.cpu().numpy()
+        return out
+    return enc
+
+
+# ------------------------------------------------------------------------------------------------ reference arm
+def run_reference(args):
+    rank, world, _ = rank_info()
+    if rank != 0:
+        return
+    import oracle
+    from veckern_b200 import configs
+
+    kind = "reference" if oracle.ref_available() else "port"
+    w = configs.make(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k)
+    s = w.spec
+    cores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    if kind == "reference":
+        R = oracle.ref()
+        pq = R.pq(s["d"], s["m"])
+        pq.centroids = w.centroids
+        run = lambda q: R.adc_search(pq, w.codes, q, s["k"])  # noqa: E731
+    else:
+        P = oracle.port()
+        run = lambda q: P.adc_search(w.centroids, w.codes, q, s["k"], cores)  # noqa: E731
+    t0 = time.perf_counter()
+    run(w.queries[:max(1, min(8, s["nq"]))])
+    probe = time.perf_counter() - t0
+    per_q = probe / max(1, min(8, s["nq"]))
+    per_step = 60.0 / max(1, args.steps + args.warmup)  # the whole reference run stays near one minute
+    sample = int(max(1, min(s["nq"], per_step / max(per_q, 1e-9))))
+    for i in range(args.warmup):
+        run(w.queries[:sample])
+    times = []
+    for i in range(args.steps):
+        t0 = time.perf_counter()
+        run(w.queries[(i * sample) % s["nq"]:][:sample])
+        times.append(time.perf_counter() - t0)
+    qps = sample / float(np.mean(times))
+    line = {"impl": "reference", "metric": "queries/s", "value": round(qps, 3), "unit": "queries/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * float(np.mean(times)), 3), "higher_is_better": True,
+            "config": {"workload": workload_name(s, args.config), "n": s["n"], "m": s["m"], "nq_sample": sample,
+                       "k": s["k"]},
+            "dtype": "f32", "data": "synthetic",
+            "cpu_baseline": {"value": round(qps, 3), "unit": "queries/s", "cores": cores, "kind": kind,
+                             "sample": f"{sample} of {s['nq']} queries per step, full database of {s['n']} rows"},
+            "e2e": {"value": round(qps, 3), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_name(s, cfg):
+    return f"{cfg}: flat PQ search n={s['n']:,} d={s['d']} m={s['m']} nq={s['nq']:,} k={s['k']}"
+
+
+# ------------------------------------------------------------------------------------------------ our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from veckern_b200 import PQSearcher, Tuning, device_info, merge_topk_device
+
+    rank, world, local = rank_info()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    spec, w = build_workload(args, rank, world)
+    n, m, nq, k = spec["n"], spec["m"], spec["nq"], spec["k"]
+    shard = math.ceil(n / world)
+    lo, hi = rank * shard, min(n, (rank + 1) * shard)
+    tuning = Tuning(queries_per_block=args.qpb, vectors_per_step=args.ilp)
+    if w.codes is not None:
+        s = PQSearcher(w.centroids, w.codes[lo:hi], device=local, id_base=lo)
+    else:
+        s = PQSearcher.generated(w.centroids, spec["code_seed"], w.cdf, lo, hi - lo, device=local, id_base=lo)
+    s.set_tuning(tuning)
+
+    stream = torch.cuda.current_stream()
+    d_q = torch.from_numpy(w.queries).cuda()
+    d_local = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+    d_gather = torch.empty((world, nq, k), dtype=torch.int64, device="cuda") if world > 1 else None
+    d_final = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def step_device():
+        s.search_device(d_q, k, d_local, stream)
+        if world > 1:
+            dist.all_gather_into_tensor(d_gather, d_local)
+            merge_topk_device(local, d_gather, nq, world, k, k, nq * k, k, d_final, stream)
+
+    for _ in range(args.warmup):
+        step_device()
+    s.sync(stream)
+    torch.cuda.synchronize()
+
+    # ---- value: device-resident steps
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        step_device()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s.sync(stream)
+    dev_ms = sum(a.elapsed_time(b) for a, b in ev)
+
+    # ---- e2e: the host-buffer C-ABI call (vk_search), rank-local; N > 1 adds gather + merge + result copy
+    h_q = torch.from_numpy(w.queries).pin_memory().numpy()
+    from veckern_b200 import NEIGHBOR_DTYPE
+    h_out = torch.empty((nq, k), dtype=torch.int64).pin_memory().numpy().view(NEIGHBOR_DTYPE)
+    h_final = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+    e2e_ms, scan_ms, lut_ms, sel_ms = [], [], [], []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        _, t = s.search(h_q, k, out=h_out)  # synchronous: H2D, LUT, scan, merge, D2H
+        if world > 1:
+            d_local.copy_(torch.from_numpy(h_out.view(np.int64)), non_blocking=True)
+            dist.all_gather_into_tensor(d_gather, d_local)
+            merge_topk_device(local, d_gather, nq, world, k, k, nq * k, k, d_final, stream)
+            h_final.copy_(d_final, non_blocking=True)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        total = t0.elapsed_time(t1)
+        if i >= args.warmup:
+            e2e_ms.append(total)
+            scan_ms.append(t.scan_ms)
+            lut_ms.append(t.lut_ms)
+            sel_ms.append(t.select_ms)
+    clk = clocks.stop()
+
+    dev_ms_t = torch.tensor([dev_ms, float(np.sum(e2e_ms)), float(np.mean(scan_ms))], device="cuda")
+    if world > 1:
+        dist.all_reduce(dev_ms_t, op=dist.ReduceOp.MAX)
+    dev_ms, e2e_total, scan_mean = dev_ms_t.tolist()
+
+    if rank == 0:
+        ms_step = dev_ms / args.steps
+        value = nq / (ms_step / 1e3)
+        e2e_value = nq / (e2e_total / args.steps / 1e3)
+        info = device_info(local)
+        sm_mhz = clk.get("sm_mhz") or info.clock_mhz
+        lookups = float(nq) * (hi - lo) * m  # per rank (rank 0's shard) per launch
+        achieved = lookups / (scan_mean / 1e3)
+        smem_peak_bytes = 128.0 * info.sm_count * sm_mhz * 1e6
+        Q = s.last_launch().queries_per_block
+        codes_for_model = w.codes[lo:hi] if w.codes is not None else None
+        wf = lookup_wavefront_model(codes_for_model, Q) if codes_for_model is not None else None
+        per_fetch = 4 if Q >= 4 else Q  # lookups served per warp LUT fetch per lane
+        fetches = lookups / 32.0 / per_fetch
+        floor_ms = fetches * wf / (info.sm_count * sm_mhz * 1e6) * 1e3 if wf else None
+        roofline = {
+            "bound": "smem",
+            "achieved": round(achieved * 4 / 1e9, 1), "peak": round(smem_peak_bytes / 1e9, 1), "unit": "GB/s",
+            "frac": round(achieved * 4 / smem_peak_bytes, 4),
+            "traffic": None,
+            "note": ("achieved = algorithmic LUT bytes (4 B per (query, row, sub-space) lookup) / scan-kernel event "
+                     "time; peak = shared-memory bandwidth 128 B/clk/SM x SMs x median SM clock sampled under load"),
+            "lookup_floor": {"wavefronts_per_fetch": round(wf, 3) if wf else None,
+                             "floor_ms": round(floor_ms, 4) if floor_ms else None,
+                             "kernel_ms": round(scan_mean, 4),
+                             "frac": round(floor_ms / scan_mean, 4) if floor_ms else None},
+            "hbm": {"code_bytes_per_launch": int((hi - lo) * m), "peak_gbs_measured": _peak("hbm_gbs")},
+        }
+        cpu = None if args.no_cpu_baseline else cpu_baseline(args, w, spec)
+        line = {
+            "metric": "queries/s", "value": round(value, 1), "unit": "queries/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": workload_name(spec, args.config), "n": n, "d": spec["d"], "m": m, "nq": nq,
+                       "k": k, "queries_per_block": Q, "vectors_per_step": s.last_launch().vectors_per_step,
+                       "shards": world, "l2": "flushed (256 MB write) before every timed step",
+                       "parallelism": f"id-sharded x{world}" if world > 1 else "single GPU"},
+            "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
+                    "h2d_bytes_per_step": int(w.queries.nbytes), "d2h_bytes_per_step": int(nq * k * 8),
+                    "stages_ms": {"lut": round(float(np.mean(lut_ms)), 4), "scan": round(scan_mean, 4),
+                                  "select": round(float(np.mean(sel_ms)), 4)}},
+            "gpu_launches": args.steps * (3 + (1 if world > 1 else 0)),
+            "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _peak(key):
+    try:
+        return json.loads((REPO / "MEASURED_PEAKS.json").read_text()).get(key)
+    except Exception:
+        return None
+
+
+def cpu_baseline(args, w, spec):
+    """The reference's adc_search on this host, bounded to about --cpu-seconds of work (rank 0, N = 1 only)."""
+    import oracle
+
+    if int(os.environ.get("WORLD_SIZE", 1)) > 1:
+        return None
+    cores = os.cpu_count() or 1
+    kind = "reference" if oracle.ref_available() else "port"
+    if kind == "reference":
+        R = oracle.ref()
+        pq = R.pq(spec["d"], spec["m"])
+        pq.centroids = w.centroids
+        run = lambda q: R.adc_search(pq, w.codes, q, spec["k"])  # noqa: E731
+    else:
+        P = oracle.port()
+        run = lambda q: P.adc_search(w.centroids, w.codes, q, spec["k"], cores)  # noqa: E731
+    t0 = time.perf_counter()
+    run(w.queries[:cores])
+    per_q = (time.perf_counter() - t0) / cores
+    sample = int(max(cores, min(spec["nq"], args.cpu_seconds / max(per_q, 1e-9))))
+    t0 = time.perf_counter()
+    run(w.queries[:sample])
+    dt = time.perf_counter() - t0
+    return {"value": round(sample / dt, 2), "unit": "queries/s", "cores": cores, "kind": kind,
+            "sample": f"{sample} of {spec['nq']} queries over the full {spec['n']:,}-row database ({dt:.1f} s)"}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,171 @@
+/*
+ * VecKern-B200 C ABI: flat PQ search (per-query L2 LUT -> ADC scan over uint8 codes -> k-smallest selection)
+ * on NVIDIA B200 (sm_100a). Plain pointers and sizes only; no CUDA or C++ types cross this boundary.
+ *
+ * Every entry point returns an int status (VK_OK = 0, negative on error); vk_last_error() gives the message of
+ * the calling thread's last failure. The C++ class veckern::gpu::PQSearcher (include/veckern/gpu.hpp) is a thin
+ * wrapper over these functions that rethrows failures as std::runtime_error, which is the reference's error
+ * convention (src/cuda/searcher.cu:11-16, include/veckern/common.hpp:23-25).
+ *
+ * Results are bit-identical to the reference CPU path (src/cpu/cpu_ref.cpp:38-54): fp32 LUT entries summed over
+ * j without FMA contraction, distances summed over sub-spaces s = 0..m-1 in order, and the k smallest
+ * (dist, id) pairs with ties broken by the lower id, ascending, padded with {+inf, -1}.
+ * Inputs must be finite: NaN distances are never returned (the reference's heap keeps them in arbitrary order).
+ *
+ * Thread safety: one index may be used by one host thread at a time (as the reference's PQSearcher).
+ */
+#ifndef VK_ABI_H
+#define VK_ABI_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    VK_OK = 0,
+    VK_ERR_INVALID = -1,     /* bad argument (the reference throws std::runtime_error from check()) */
+    VK_ERR_CUDA = -2,        /* a CUDA runtime call failed */
+    VK_ERR_NOMEM = -3,       /* device allocation failed */
+    VK_ERR_DEVICE = -4,      /* a kernel reported an error through its status word (e.g. a bounded wait ran out) */
+    VK_ERR_UNSUPPORTED = -5  /* configuration this build does not implement */
+};
+
+/* Scan variants of the reference API (include/veckern/gpu.hpp:13-23). They select validation rules only: every
+ * search runs the one fused B200 kernel, every distances() call the one materialising scan. */
+enum {
+    VK_VARIANT_GLOBAL_LUT = 0,
+    VK_VARIANT_SHARED_LUT = 1,
+    VK_VARIANT_SHARED_LUT_VEC = 2,
+    VK_VARIANT_INTERLEAVED = 3,
+    VK_VARIANT_FUSED = 4,
+    VK_VARIANT_FUSED_REG = 5,
+    VK_VARIANT_FUSED_VEC = 6,
+    VK_VARIANT_FUSED_VEC_MQ = 7,
+    VK_VARIANT_FUSED_WARP = 8
+};
+
+/* One result: the reference's veckern::Neighbor (include/veckern/common.hpp:13-16), same 8-byte layout. */
+typedef struct {
+    float dist;
+    int32_t id;
+} vk_neighbor_t;
+
+/* Replaces gpu::DeviceInfo (include/veckern/gpu.hpp:36-41). */
+typedef struct {
+    char name[256];
+    int sm_count;
+    double peak_bandwidth_gbs;  /* 2 x memory clock x bus width */
+    size_t max_smem_per_block;  /* opt-in limit */
+    int clock_mhz;              /* max SM clock */
+} vk_device_info_t;
+
+/* Replaces gpu::Tuning (include/veckern/gpu.hpp:29-34) with the same meaning and the same accepted values
+ * (src/cuda/searcher.cu:450-460): scan_threads multiple of 32 in [32, 1024] (used by distances()),
+ * blocks_per_query >= 0 (vector chunks per query group; 0 = auto), queries_per_block in {1, 2, 4, 8},
+ * vectors_per_step in {1, 2, 4} (32-vector groups each warp holds in flight). */
+typedef struct {
+    int scan_threads;
+    int blocks_per_query;
+    int queries_per_block;
+    int vectors_per_step;
+} vk_tuning_t;
+
+/* Replaces gpu::Timings (include/veckern/gpu.hpp:46-50): milliseconds per stage from CUDA events. */
+typedef struct {
+    double transfer_ms, lut_ms, scan_ms, select_ms;
+} vk_timings_t;
+
+/* Replaces PQSearcher::LaunchShape (include/veckern/gpu.hpp:68-73). For the fused kernel: threads = block size,
+ * blocks_x = vector chunks per query group, grid_y = query groups (ceil(nq / Q)), blocks_per_sm from the
+ * occupancy API, waves = work items / resident blocks. */
+typedef struct {
+    int threads, blocks_x, grid_y, queries_per_block, vectors_per_step, blocks_per_sm;
+    double waves;
+} vk_launch_shape_t;
+
+typedef struct vk_index vk_index_t;
+
+/* Replaces gpu::device_info (src/cuda/searcher.cu:143-156). */
+int vk_device_info(int device, vk_device_info_t* out);
+
+/* Copies the message of this thread's last failure into buf (NUL-terminated); returns its full length. */
+size_t vk_last_error(char* buf, size_t len);
+
+/* Tuning defaults and validation (include/veckern/gpu.hpp:29-34, src/cuda/searcher.cu:450-460). */
+void vk_tuning_default(vk_tuning_t* t);
+int vk_tuning_validate(const vk_tuning_t* t);
+
+/* Replaces the PQSearcher constructor (src/cuda/searcher.cu:427-444): copies centroids ([m][256][dsub] fp32) and
+ * row-major n x m codes from HOST memory to `device` and builds the 16-byte-word-interleaved layout there.
+ * Ids reported by searches are id_base + row (id_base + n must fit in int32, as the reference's n < INT_MAX
+ * check, src/cuda/searcher.cu:430). */
+int vk_index_create(int device, const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
+                    int64_t id_base, vk_index_t** out);
+
+/* Same, with the row-major codes already in DEVICE memory of `device` (e.g. produced by vk_encode_device). */
+int vk_index_create_from_device(int device, const float* centroids, int m, int dsub, const uint8_t* d_codes,
+                                int64_t n, int64_t id_base, vk_index_t** out);
+
+/* Synthetic code database generated directly on the device (BASELINE configs 3/4): rows
+ * [row_first, row_first + n) of the generator `vk_gen_codes_host` (veckern_b200 host library) defines. cdf is
+ * the host-computed [clusters][m][256] uint32 categorical table. Ids are id_base + (row - row_first). */
+int vk_index_create_generated(int device, const float* centroids, int m, int dsub, uint64_t seed,
+                              const uint32_t* cdf, int clusters, int64_t row_first, int64_t n, int64_t id_base,
+                              vk_index_t** out);
+
+/* Replaces ~PQSearcher. */
+int vk_index_destroy(vk_index_t* index);
+
+/* Basic facts about an index: n, m, dsub, id_base, device. Any pointer may be NULL. */
+int vk_index_info(const vk_index_t* index, int64_t* n, int* m, int* dsub, int64_t* id_base, int* device);
+
+/* Copies the index's row-major codes for rows [first, first + count) back to host memory (tests, tools). */
+int vk_index_get_codes(const vk_index_t* index, int64_t first, int64_t count, uint8_t* out);
+
+/* Replaces PQSearcher::search (src/cuda/searcher.cu:466-520): HOST queries (nq x d fp32) in, HOST results
+ * (nq x k vk_neighbor_t, ascending) out, 1 <= k <= min(128, n). Synchronous. timings/shape may be NULL.
+ * `variant` only selects the reference's validation rules (m % 16 == 0 for variants 2, 6, 7, 8). */
+int vk_search(vk_index_t* index, const float* queries, int64_t nq, int k, int variant, const vk_tuning_t* tuning,
+              vk_neighbor_t* out, vk_timings_t* timings, vk_launch_shape_t* shape);
+
+/* Device-resident search: DEVICE queries and results on the caller's CUDA stream (cudaStream_t passed as void*;
+ * NULL = the index's own stream). Asynchronous: call vk_index_sync to wait and collect kernel status. */
+int vk_search_device(vk_index_t* index, const float* d_queries, int64_t nq, int k, const vk_tuning_t* tuning,
+                     vk_neighbor_t* d_out, void* stream);
+
+/* Waits for the index's work on `stream` (NULL = its own) and reports any kernel-side error. */
+int vk_index_sync(vk_index_t* index, void* stream);
+
+/* Replaces PQSearcher::distances (src/cuda/searcher.cu:522-547): the full nq x n ADC matrix to HOST memory.
+ * Rejected for the fused variants, as in the reference. */
+int vk_distances(vk_index_t* index, const float* queries, int64_t nq, int variant, const vk_tuning_t* tuning,
+                 float* out, vk_timings_t* timings);
+
+/* Replaces lut_kernel (src/cuda/kernels.cuh:17-30) for direct use: lut[q][s][c] (nq x m x 256 fp32) in DEVICE
+ * memory, computed on `stream` from DEVICE queries with the index's centroids. */
+int vk_compute_lut_device(vk_index_t* index, const float* d_queries, int64_t nq, float* d_lut, void* stream);
+
+/* Replaces select_kernel's role as the final reduction (src/cuda/kernels.cuh:179-202) and is the multi-GPU
+ * merge: for each of nq queries, the k best of `lists` sorted candidate lists of k_in entries each, all in DEVICE
+ * memory on `device`. Entry (q, list l, j) is at in[q * query_stride + l * list_stride + j]. Entries with
+ * id < 0 are padding and are skipped. Output: nq x k ascending, padded with {+inf, -1}. */
+int vk_merge_topk_device(int device, const vk_neighbor_t* d_in, int64_t nq, int lists, int k_in,
+                         int64_t query_stride, int64_t list_stride, int k, vk_neighbor_t* d_out, void* stream);
+
+/* Bit-exact PQ encode on the device (nearest centroid per sub-space under the reference's l2sq, first minimum
+ * wins; src/cpu/pq.cpp:11-22, 71-76): DEVICE x (n x d fp32) -> DEVICE codes (n x m). */
+int vk_encode_device(int device, const float* centroids, int m, int dsub, const float* d_x, int64_t n,
+                     uint8_t* d_codes, void* stream);
+
+/* Generates rows [row_first, row_first + n) of the synthetic code generator into DEVICE memory (row-major n x m);
+ * the same integers as vk_gen_codes_host. */
+int vk_gen_codes_device(int device, uint64_t seed, const uint32_t* cdf, int clusters, int m, int64_t row_first,
+                        int64_t n, uint8_t* d_codes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VK_ABI_H */

@@ -1,0 +1,265 @@
+"""ctypes wrappers for the CPU checkers — TEST INFRASTRUCTURE ONLY (see oracle/__init__.py).
+
+Port: the plain-C restatement of the reference CPU path (oracle/vk_oracle.c, built to oracle/_build/).
+Ref:  the reference's own CPU sources + oracle/ref_shim.cpp (built to oracle/_ref/ by oracle/Makefile).
+All arrays are numpy, C-contiguous; results come back as (dists float32 [nq, k], ids int32 [nq, k]).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+PORT_SO = HERE / "_build" / "libvk_oracle.so"
+REF_SO = HERE / "_ref" / "libveckern_ref.so"
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_i64 = C.c_int64
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _u8(a):
+    return np.ascontiguousarray(a, dtype=np.uint8)
+
+
+class Port:
+    """The plain-C restatement (kind "port")."""
+
+    def __init__(self, path: Path = PORT_SO):
+        if not path.exists():
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle oracle` (or __graft_entry__.build())")
+        L = self.lib = C.CDLL(str(path))
+        L.vko_compute_lut.argtypes = [_f32p, C.c_int, C.c_int, _f32p, _i64, _f32p]
+        L.vko_adc_scan.argtypes = [_f32p, _i64, _u8p, _i64, C.c_int, _f32p]
+        L.vko_select_topk.argtypes = [_f32p, _i64, _i64, C.c_int, _f32p, _i32p]
+        L.vko_adc_search.argtypes = [_f32p, C.c_int, C.c_int, _u8p, _i64, _f32p, _i64, C.c_int, _f32p, _i32p,
+                                     C.c_int]
+        L.vko_topk_push_all.argtypes = [_f32p, _i32p, _i64, C.c_int, _f32p, _i32p]
+        L.vko_merge_topk.argtypes = [_f32p, _i32p, C.c_int, _i64, C.c_int, _f32p, _i32p]
+        L.vko_recall_at_k.argtypes = [_i32p, _i64, _i32p, _i64, _i64, C.c_int]
+        L.vko_recall_at_k.restype = C.c_double
+        L.vko_stream_create.argtypes = [_f32p, _i64, C.c_int, C.c_int]
+        L.vko_stream_create.restype = C.c_void_p
+        L.vko_stream_feed.argtypes = [C.c_void_p, _u8p, _i64, _i64, C.c_int]
+        L.vko_stream_finish.argtypes = [C.c_void_p, _f32p, _i32p]
+        L.vko_stream_destroy.argtypes = [C.c_void_p]
+
+    def compute_lut(self, centroids, queries):
+        centroids = _f32(centroids)
+        m, ksub, dsub = centroids.shape
+        queries = _f32(queries).reshape(-1, m * dsub)
+        lut = np.empty((queries.shape[0], m, 256), np.float32)
+        self.lib.vko_compute_lut(centroids, m, dsub, queries, queries.shape[0], lut)
+        return lut
+
+    def adc_scan(self, lut, codes):
+        lut = _f32(lut)
+        codes = _u8(codes)
+        nq, m = lut.shape[0], lut.shape[1]
+        n = codes.shape[0]
+        out = np.empty((nq, n), np.float32)
+        self.lib.vko_adc_scan(lut, nq, codes, n, m, out)
+        return out
+
+    def select_topk(self, dists, k):
+        dists = _f32(dists)
+        nq, n = dists.shape
+        d = np.empty((nq, k), np.float32)
+        i = np.empty((nq, k), np.int32)
+        self.lib.vko_select_topk(dists, nq, n, k, d, i)
+        return d, i
+
+    def adc_search(self, centroids, codes, queries, k, threads=0):
+        centroids = _f32(centroids)
+        m, _, dsub = centroids.shape
+        codes = _u8(codes)
+        queries = _f32(queries).reshape(-1, m * dsub)
+        nq = queries.shape[0]
+        d = np.empty((nq, k), np.float32)
+        i = np.empty((nq, k), np.int32)
+        self.lib.vko_adc_search(centroids, m, dsub, codes, codes.shape[0], queries, nq, k, d, i, threads)
+        return d, i
+
+    def topk_push_all(self, dists, ids, k):
+        dists = _f32(dists)
+        ids = np.ascontiguousarray(ids, np.int32)
+        d = np.empty(k, np.float32)
+        i = np.empty(k, np.int32)
+        self.lib.vko_topk_push_all(dists, ids, dists.shape[0], k, d, i)
+        return d, i
+
+    def merge_topk(self, d, ids, k):
+        """d, ids: [nq, lists, k] -> the k best of the union per query."""
+        d = _f32(d)
+        ids = np.ascontiguousarray(ids, np.int32)
+        nq, lists = d.shape[0], d.shape[1]
+        od = np.empty((nq, k), np.float32)
+        oi = np.empty((nq, k), np.int32)
+        self.lib.vko_merge_topk(d, ids, lists, nq, k, od, oi)
+        return od, oi
+
+    def recall_at_k(self, found, truth, k):
+        found = np.ascontiguousarray(found, np.int32)
+        truth = np.ascontiguousarray(truth, np.int32)
+        return self.lib.vko_recall_at_k(found, found.shape[1], truth, truth.shape[1], found.shape[0], k)
+
+    def stream_search(self, lut, code_blocks, k, threads=0):
+        """code_blocks: iterable of (codes [count, m] uint8, id_base). Returns the top-k over all blocks."""
+        lut = _f32(lut)
+        nq, m = lut.shape[0], lut.shape[1]
+        s = self.lib.vko_stream_create(lut, nq, m, k)
+        try:
+            for codes, base in code_blocks:
+                codes = _u8(codes)
+                self.lib.vko_stream_feed(s, codes, codes.shape[0], base, threads)
+            d = np.empty((nq, k), np.float32)
+            i = np.empty((nq, k), np.int32)
+            self.lib.vko_stream_finish(s, d, i)
+            return d, i
+        finally:
+            self.lib.vko_stream_destroy(s)
+
+
+class Ref:
+    """The reference's own CPU library (kind "reference"); present only where it was built."""
+
+    def __init__(self, path: Path = REF_SO):
+        if not path.exists():
+            raise FileNotFoundError(f"{path} missing: built by `make -C oracle ref` where the reference exists")
+        L = self.lib = C.CDLL(str(path))
+        L.ref_pq_create.argtypes = [_i64, _i64]
+        L.ref_pq_create.restype = C.c_void_p
+        L.ref_pq_destroy.argtypes = [C.c_void_p]
+        L.ref_pq_train.argtypes = [C.c_void_p, _f32p, _i64, _i64, C.c_uint64]
+        L.ref_pq_encode.argtypes = [C.c_void_p, _f32p, _i64, _u8p]
+        L.ref_pq_decode.argtypes = [C.c_void_p, _u8p, _i64, _f32p]
+        L.ref_pq_get_centroids.argtypes = [C.c_void_p, _f32p]
+        L.ref_pq_set_centroids.argtypes = [C.c_void_p, _f32p]
+        L.ref_compute_lut.argtypes = [C.c_void_p, _f32p, _i64, _f32p]
+        L.ref_adc_scan.argtypes = [_f32p, _i64, _u8p, _i64, _i64, _f32p]
+        L.ref_select_topk.argtypes = [_f32p, _i64, _i64, _i64, _f32p, _i32p]
+        L.ref_adc_search.argtypes = [C.c_void_p, _u8p, _i64, _f32p, _i64, _i64, _f32p, _i32p]
+        L.ref_exact_knn.argtypes = [_f32p, _i64, _f32p, _i64, _i64, _i64, _f32p, _i32p]
+        L.ref_topk_push_all.argtypes = [_f32p, _i32p, _i64, _i64, _f32p, _i32p]
+        L.ref_synthetic_clustered.argtypes = [_i64, _i64, _i64, C.c_uint64, _f32p]
+
+    class PQ:
+        def __init__(self, lib, d, m):
+            self.lib, self.d, self.m, self.dsub = lib, d, m, d // m
+            self.h = lib.ref_pq_create(d, m)
+
+        def __del__(self):
+            if getattr(self, "h", None):
+                self.lib.ref_pq_destroy(self.h)
+                self.h = None
+
+        def train(self, x, n, iters, seed=1):
+            self.lib.ref_pq_train(self.h, _f32(x), n, iters, seed)
+
+        def encode(self, x):
+            x = _f32(x).reshape(-1, self.d)
+            codes = np.empty((x.shape[0], self.m), np.uint8)
+            self.lib.ref_pq_encode(self.h, x, x.shape[0], codes)
+            return codes
+
+        def decode(self, codes):
+            codes = _u8(codes)
+            x = np.empty((codes.shape[0], self.d), np.float32)
+            self.lib.ref_pq_decode(self.h, codes, codes.shape[0], x)
+            return x
+
+        @property
+        def centroids(self):
+            c = np.empty((self.m, 256, self.dsub), np.float32)
+            self.lib.ref_pq_get_centroids(self.h, c)
+            return c
+
+        @centroids.setter
+        def centroids(self, c):
+            self.lib.ref_pq_set_centroids(self.h, _f32(c))
+
+    def pq(self, d, m):
+        return Ref.PQ(self.lib, d, m)
+
+    def compute_lut(self, pq, queries):
+        queries = _f32(queries).reshape(-1, pq.d)
+        lut = np.empty((queries.shape[0], pq.m, 256), np.float32)
+        self.lib.ref_compute_lut(pq.h, queries, queries.shape[0], lut)
+        return lut
+
+    def adc_scan(self, lut, codes):
+        lut = _f32(lut)
+        codes = _u8(codes)
+        out = np.empty((lut.shape[0], codes.shape[0]), np.float32)
+        self.lib.ref_adc_scan(lut, lut.shape[0], codes, codes.shape[0], lut.shape[1], out)
+        return out
+
+    def select_topk(self, dists, k):
+        dists = _f32(dists)
+        d = np.empty((dists.shape[0], k), np.float32)
+        i = np.empty((dists.shape[0], k), np.int32)
+        self.lib.ref_select_topk(dists, dists.shape[0], dists.shape[1], k, d, i)
+        return d, i
+
+    def adc_search(self, pq, codes, queries, k):
+        codes = _u8(codes)
+        queries = _f32(queries).reshape(-1, pq.d)
+        nq = queries.shape[0]
+        d = np.empty((nq, k), np.float32)
+        i = np.empty((nq, k), np.int32)
+        self.lib.ref_adc_search(pq.h, codes, codes.shape[0], queries, nq, k, d, i)
+        return d, i
+
+    def exact_knn(self, base, queries, k):
+        base = _f32(base)
+        queries = _f32(queries)
+        nq, dim = queries.shape
+        d = np.empty((nq, k), np.float32)
+        i = np.empty((nq, k), np.int32)
+        self.lib.ref_exact_knn(base, base.shape[0], queries, nq, dim, k, d, i)
+        return d, i
+
+    def topk_push_all(self, dists, ids, k):
+        d = np.empty(k, np.float32)
+        i = np.empty(k, np.int32)
+        self.lib.ref_topk_push_all(_f32(dists), np.ascontiguousarray(ids, np.int32), len(dists), k, d, i)
+        return d, i
+
+    def synthetic_clustered(self, n, d, clusters, seed):
+        out = np.empty((n, d), np.float32)
+        self.lib.ref_synthetic_clustered(n, d, clusters, seed, out)
+        return out
+
+
+_port = None
+_ref = None
+
+
+def port() -> Port:
+    global _port
+    if _port is None:
+        _port = Port()
+    return _port
+
+
+def ref_available() -> bool:
+    return REF_SO.exists()
+
+
+def ref() -> Ref:
+    global _ref
+    if _ref is None:
+        _ref = Ref()
+    return _ref
+
+
+def set_threads(n: int) -> None:
+    os.environ["OMP_NUM_THREADS"] = str(n)

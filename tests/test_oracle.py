@@ -1,0 +1,113 @@
+"""CPU: the oracle (plain-C restatement of the reference CPU path) against the reference's own outputs.
+
+The golden fixtures were produced by running the reference's CPU library (tests/golden/make_golden.py); where that
+library is built here (oracle/_ref), the oracle is also compared with it directly on fresh random inputs.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from conftest import assert_same_topk, bits
+
+
+def test_topk_known_answer(port, golden):
+    g = golden("topk_kat")
+    d, i = port.topk_push_all(g["kat_values"], np.arange(5, dtype=np.int32), 3)
+    assert list(i) == [1, 3, 4]  # tie on 1.0 broken by the lower id (reference tests/test_cpu.cpp:33-41)
+    assert np.array_equal(bits(d), bits(g["kat_d"])) and np.array_equal(i, g["kat_i"])
+    d, i = port.topk_push_all(np.array([2.0], np.float32), np.array([9], np.int32), 4)
+    assert list(i) == [9, -1, -1, -1] and np.isinf(d[1:]).all()  # padding (tests/test_cpu.cpp:42-45)
+    for r, k in enumerate(g["seq_k"]):
+        d, i = port.topk_push_all(g["seq_v"][r], g["seq_i"][r], int(k))
+        assert np.array_equal(i, g["seq_out_i"][r, :k]) and np.array_equal(bits(d), bits(g["seq_out_d"][r, :k]))
+
+
+def test_cpu_fixture_lut_scan_search(port, golden):
+    g = golden("cpu_fixture")
+    lut = port.compute_lut(g["centroids"], g["queries"])
+    assert np.array_equal(bits(lut), bits(g["lut"]))
+    dists = port.adc_scan(lut, g["codes"])
+    assert np.array_equal(bits(dists), bits(g["dists"]))
+    d, i = port.adc_search(g["centroids"], g["codes"], g["queries"], 10)
+    assert_same_topk(d, i, g["top_d"], g["top_i"], "cpu fixture")
+
+
+def test_staged_equals_fused(port, golden):
+    """The reference's only exact-equality CPU test (tests/test_cpu.cpp:84-94): LUT+scan+select == adc_search."""
+    g = golden("cpu_fixture")
+    lut = port.compute_lut(g["centroids"], g["queries"])
+    sd, si = port.select_topk(port.adc_scan(lut, g["codes"]), 10)
+    fd, fi = port.adc_search(g["centroids"], g["codes"], g["queries"], 10)
+    assert_same_topk(sd, si, fd, fi, "staged vs fused")
+
+
+@pytest.mark.parametrize("k", [1, 8, 10, 16, 32, 33, 64, 100, 128])
+def test_gpu_fixture_all_k(port, golden, k):
+    g = golden("gpu_fixture")
+    d, i = port.adc_search(g["centroids"], g["codes"], g["queries"], k)
+    assert_same_topk(d, i, g[f"d_k{k}"], g[f"i_k{k}"], f"k={k}")
+
+
+def test_c0_pipeline_small(port, golden):
+    """Config 0's pipeline (N(0,1) rows, PQ from 256 rows picked with seed 1, encode) reproduces the reference's
+    codebook, codes and results."""
+    from veckern_b200 import data
+
+    g = golden("c0_small")
+    x = data.gen_normal(0, 20_000, 128)
+    q = data.gen_normal(2, 100, 128)
+    assert np.array_equal(bits(q), bits(g["queries"]))
+    cent = data.pq_train(x, 16, 0, 1)
+    assert np.array_equal(bits(cent), bits(g["centroids"]))
+    assert np.array_equal(data.pq_encode(cent, x), g["codes"])
+    d, i = port.adc_search(cent, g["codes"], q, 10)
+    assert_same_topk(d, i, g["top_d"], g["top_i"], "c0 small")
+
+
+@pytest.mark.parametrize("k", [10, 100])
+def test_exact_ties(port, golden, k):
+    g = golden("ties")
+    d, i = port.adc_search(g["centroids"], g["codes"], g["queries"], k)
+    assert_same_topk(d, i, g[f"d_k{k}"], g[f"i_k{k}"], f"ties k={k}")
+    # the fixture really has ties, broken by id
+    assert (np.diff(g[f"d_k{k}"], axis=1) == 0).sum() > 0
+
+
+def test_merge_of_shards_equals_unsharded(port, golden):
+    g = golden("gpu_fixture")
+    n = g["codes"].shape[0]
+    k = 33
+    bounds = [0, 5000, 5001, 12_345, n]
+    parts_d, parts_i = [], []
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        d, i = port.adc_search(g["centroids"], g["codes"][a:b], g["queries"], k)
+        parts_d.append(d)
+        parts_i.append(np.where(i >= 0, i + a, -1).astype(np.int32))
+    d = np.stack(parts_d, axis=1)
+    i = np.stack(parts_i, axis=1)
+    md, mi = port.merge_topk(d, i, k)
+    assert_same_topk(md, mi, g[f"d_k{k}"], g[f"i_k{k}"], "merged shards")
+
+
+def test_stream_search_equals_search(port, golden):
+    g = golden("gpu_fixture")
+    lut = port.compute_lut(g["centroids"], g["queries"])
+    codes = g["codes"]
+    blocks = [(codes[a:a + 4096], a) for a in range(0, codes.shape[0], 4096)]
+    d, i = port.stream_search(lut, blocks, 100)
+    assert_same_topk(d, i, g["d_k100"], g["i_k100"], "stream")
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="reference library not built here")
+@pytest.mark.parametrize("seed,n,m,dsub,nq,k", [(1, 3001, 4, 8, 5, 7), (2, 999, 16, 2, 3, 128), (3, 257, 3, 5, 4, 1)])
+def test_port_matches_reference_random(port, seed, n, m, dsub, nq, k):
+    R = oracle.ref()
+    rng = np.random.default_rng(seed)
+    pq = R.pq(m * dsub, m)
+    pq.centroids = rng.normal(size=(m, 256, dsub)).astype(np.float32)
+    codes = rng.integers(0, 256, size=(n, m)).astype(np.uint8)
+    q = rng.normal(size=(nq, m * dsub)).astype(np.float32)
+    assert np.array_equal(bits(R.compute_lut(pq, q)), bits(port.compute_lut(pq.centroids, q)))
+    rd, ri = R.adc_search(pq, codes, q, k)
+    pd, pi = port.adc_search(pq.centroids, codes, q, k)
+    assert_same_topk(pd, pi, rd, ri, "port vs reference")

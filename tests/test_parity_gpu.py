@@ -1,0 +1,198 @@
+"""GPU parity: the sm_100a search path, called through the C ABI, against the CPU oracle and the reference's
+golden outputs. The bar is bit-exact distances and identical ids (ties to the lower id).
+
+Mirrors the reference's GPU suite (tests/test_gpu.cpp) with its tolerances tightened to equality, plus edge cases
+(ragged n, n < 32, k = n, nq = 0/1/prime, m not a multiple of 16, exact ties, every Q / ILP / S template).
+"""
+import numpy as np
+import pytest
+
+from conftest import assert_same_topk, bits
+from veckern_b200 import PQSearcher, ScanVariant, Tuning, VkError, device_info
+
+pytestmark = pytest.mark.gpu
+
+FUSED = [ScanVariant.Fused, ScanVariant.FusedReg, ScanVariant.FusedVec, ScanVariant.FusedVecMQ,
+         ScanVariant.FusedWarp]
+SCANS = [ScanVariant.GlobalLut, ScanVariant.SharedLut, ScanVariant.SharedLutVec, ScanVariant.Interleaved]
+
+
+def random_db(seed, n, m, dsub, nq, dup_rows=0):
+    rng = np.random.default_rng(seed)
+    cent = rng.normal(size=(m, 256, dsub)).astype(np.float32)
+    codes = rng.integers(0, 256, size=(n, m)).astype(np.uint8)
+    if dup_rows:
+        codes = codes[rng.integers(0, dup_rows, size=n)]
+    q = rng.normal(size=(nq, m * dsub)).astype(np.float32)
+    return cent, codes, q
+
+
+def gpu_search(cent, codes, q, k, variant=ScanVariant.FusedWarp, tuning=None):
+    with PQSearcher(cent, codes) as s:
+        if tuning:
+            s.set_tuning(tuning)
+        out, _ = s.search(q, k, variant)
+        return out["dist"].copy(), out["id"].copy(), s.last_launch()
+
+
+def test_device_info():
+    info = device_info(0)
+    assert info.sm_count > 0 and info.peak_bandwidth_gbs > 0 and info.max_smem_per_block >= 200 * 1024
+    print(f"{info.name}: {info.sm_count} SMs, {info.peak_bandwidth_gbs:.0f} GB/s, {info.clock_mhz} MHz")
+
+
+@pytest.mark.parametrize("k", [1, 8, 10, 16, 32, 33, 64, 100, 128])
+def test_golden_gpu_fixture(golden, k):
+    g = golden("gpu_fixture")
+    d, i, _ = gpu_search(g["centroids"], g["codes"], g["queries"], k)
+    assert_same_topk(d, i, g[f"d_k{k}"], g[f"i_k{k}"], f"k={k}")
+
+
+def test_golden_cpu_fixture_m8(golden):
+    """m = 8: the fused (non word-interleaved) variants accept it; results match the reference exactly."""
+    g = golden("cpu_fixture")
+    for v in [ScanVariant.GlobalLut, ScanVariant.SharedLut, ScanVariant.Interleaved, ScanVariant.Fused,
+              ScanVariant.FusedReg]:
+        d, i, _ = gpu_search(g["centroids"], g["codes"], g["queries"], 10, v)
+        assert_same_topk(d, i, g["top_d"], g["top_i"], str(v))
+
+
+def test_golden_c0_small(golden):
+    g = golden("c0_small")
+    d, i, _ = gpu_search(g["centroids"], g["codes"], g["queries"], 10)
+    assert_same_topk(d, i, g["top_d"], g["top_i"], "c0 small")
+
+
+@pytest.mark.parametrize("k", [10, 100])
+@pytest.mark.parametrize("q", [1, 2, 4, 8])
+def test_golden_ties(golden, k, q):
+    g = golden("ties")
+    d, i, _ = gpu_search(g["centroids"], g["codes"], g["queries"], k, tuning=Tuning(queries_per_block=q))
+    assert_same_topk(d, i, g[f"d_k{k}"], g[f"i_k{k}"], f"ties k={k} Q={q}")
+
+
+def test_distances_every_scan_variant(golden, port):
+    """Reference tests/test_gpu.cpp:69-79, bit-exact: the materialising scan equals the CPU ADC matrix."""
+    g = golden("gpu_fixture")
+    lut = port.compute_lut(g["centroids"], g["queries"])
+    expected = port.adc_scan(lut, g["codes"])
+    with PQSearcher(g["centroids"], g["codes"]) as s:
+        for v in SCANS:
+            got, _ = s.distances(g["queries"], v)
+            assert np.array_equal(bits(got), bits(expected)), v
+        for threads in (64, 128, 512):
+            s.set_tuning(Tuning(scan_threads=threads))
+            got, _ = s.distances(g["queries"], ScanVariant.SharedLut)
+            assert np.array_equal(bits(got), bits(expected))
+        with pytest.raises(VkError):
+            s.distances(g["queries"], ScanVariant.FusedWarp)
+
+
+def test_distances_cpu_fixture_m8(golden):
+    g = golden("cpu_fixture")
+    with PQSearcher(g["centroids"], g["codes"]) as s:
+        got, _ = s.distances(g["queries"], ScanVariant.Interleaved)
+    assert np.array_equal(bits(got), bits(g["dists"]))
+
+
+@pytest.mark.parametrize("variant", SCANS + FUSED)
+def test_all_variants_k10(golden, variant):
+    g = golden("gpu_fixture")
+    d, i, _ = gpu_search(g["centroids"], g["codes"], g["queries"], 10, variant)
+    assert_same_topk(d, i, g["d_k10"], g["i_k10"], str(variant))
+
+
+@pytest.mark.parametrize("q", [1, 2, 4, 8])
+@pytest.mark.parametrize("ilp", [1, 2, 4])
+@pytest.mark.parametrize("k", [1, 10, 33, 64, 128])
+def test_every_q_ilp_k(golden, q, ilp, k):
+    """nq = 37 is prime, so every Q > 1 leaves a partial last group (reference tests/test_gpu.cpp:93-101)."""
+    g = golden("gpu_fixture")
+    d, i, shape = gpu_search(g["centroids"], g["codes"], g["queries"], k,
+                             tuning=Tuning(queries_per_block=q, vectors_per_step=ilp))
+    assert_same_topk(d, i, g[f"d_k{k}"], g[f"i_k{k}"], f"Q={q} ILP={ilp} k={k}")
+    assert shape.queries_per_block == q and shape.grid_y == -(-37 // q)
+
+
+@pytest.mark.parametrize("bpq", [1, 3, 7, 16])
+def test_blocks_per_query_overrides(golden, bpq):
+    g = golden("gpu_fixture")
+    for ilp in (1, 4):
+        d, i, shape = gpu_search(g["centroids"], g["codes"], g["queries"], 33,
+                                 tuning=Tuning(blocks_per_query=bpq, vectors_per_step=ilp))
+        assert_same_topk(d, i, g["d_k33"], g["i_k33"], f"bpq={bpq}")
+        assert shape.blocks_x <= bpq
+
+
+def test_launch_shape_reporting(golden):
+    """Reference tests/test_gpu.cpp:131-150: default Q = 2 gives grid_y = ceil(37 / 2) = 19, and one query is
+    spread over at least min(wave, ceil(n / (threads * 16))) blocks."""
+    g = golden("gpu_fixture")
+    with PQSearcher(g["centroids"], g["codes"]) as s:
+        s.search(g["queries"], 10, ScanVariant.FusedVecMQ)
+        shape = s.last_launch()
+        assert shape.queries_per_block == 2 and shape.grid_y == 19
+        assert shape.blocks_per_sm > 0 and shape.waves > 0
+        s.search(g["queries"][:1], 10, ScanVariant.FusedWarp)
+        one = s.last_launch()
+        wave = one.blocks_x / one.waves
+        assert one.blocks_x >= min(wave, np.ceil(s.n / (one.threads * 16.0))) - 0.5
+
+
+@pytest.mark.parametrize("n,m,dsub,nq,k", [
+    (1, 16, 8, 3, 1), (31, 16, 4, 2, 31), (32, 16, 4, 5, 32), (33, 32, 2, 4, 33), (129, 64, 2, 3, 128),
+    (1000, 12, 3, 7, 10), (5003, 4, 16, 9, 100), (2047, 20, 1, 6, 17), (4099, 48, 2, 5, 64), (777, 1, 8, 3, 5),
+])
+def test_random_shapes_against_oracle(port, n, m, dsub, nq, k):
+    cent, codes, q = random_db(n * 7 + m, n, m, dsub, nq)
+    ed, ei = port.adc_search(cent, codes, q, k)
+    for variant in (ScanVariant.FusedReg, ScanVariant.SharedLut):
+        for tq in (1, 4, 8):
+            d, i, _ = gpu_search(cent, codes, q, k, variant, Tuning(queries_per_block=tq))
+            assert_same_topk(d, i, ed, ei, f"n={n} m={m} Q={tq}")
+
+
+def test_rejections(golden):
+    g = golden("gpu_fixture")
+    with PQSearcher(g["centroids"], g["codes"]) as s:
+        for k in (0, 129):
+            with pytest.raises(VkError):
+                s.search(g["queries"][:1], k, ScanVariant.Fused)
+        with pytest.raises(VkError):
+            s.set_tuning(Tuning(queries_per_block=3))
+    cg = golden("cpu_fixture")  # m = 8
+    with PQSearcher(cg["centroids"], cg["codes"]) as s:
+        for v in (ScanVariant.SharedLutVec, ScanVariant.FusedVec, ScanVariant.FusedVecMQ, ScanVariant.FusedWarp):
+            with pytest.raises(VkError):
+                s.search(cg["queries"], 10, v)
+    cent, codes, q = random_db(5, 20, 16, 2, 2)
+    with PQSearcher(cent, codes) as s:
+        with pytest.raises(VkError):
+            s.search(q, 21, ScanVariant.FusedWarp)  # k > n
+        out, _ = s.search(q, 20, ScanVariant.FusedWarp)  # k == n is fine
+        assert sorted(out["id"][0]) == list(range(20))
+
+
+def test_empty_query_batch(golden):
+    g = golden("gpu_fixture")
+    with PQSearcher(g["centroids"], g["codes"]) as s:
+        out, t = s.search(g["queries"][:0], 10)
+        assert out.shape == (0, 10) and t.total_ms() == 0
+
+
+def test_id_base_offsets_ids(port):
+    cent, codes, q = random_db(11, 3000, 16, 4, 4)
+    ed, ei = port.adc_search(cent, codes, q, 25)
+    with PQSearcher(cent, codes, id_base=1_000_000) as s:
+        out, _ = s.search(q, 25)
+    assert_same_topk(out["dist"], out["id"] - 1_000_000, ed, ei, "id_base")
+
+
+def test_repeated_searches_are_identical(golden):
+    g = golden("gpu_fixture")
+    with PQSearcher(g["centroids"], g["codes"]) as s:
+        s.set_tuning(Tuning(queries_per_block=4))
+        a, _ = s.search(g["queries"], 100)
+        for _ in range(3):
+            b, _ = s.search(g["queries"], 100)
+            assert np.array_equal(a.view(np.int64), b.view(np.int64))

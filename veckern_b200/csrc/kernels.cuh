@@ -1,0 +1,351 @@
+// VecKern-B200 kernels (sm_100a). Host dispatch lives in vk_abi.cu.
+//
+// Data layouts in HBM
+//   centroids  [m][256][dsub] fp32 (the reference's layout, include/veckern/pq.hpp:20-24)
+//   codes      16-byte-word interleaved per 32 vectors: uint4 word ((g * W + w) * 32 + l) holds sub-codes
+//              16w .. 16w+15 of vector 32g + l, W = ceil(m / 16), sub-codes >= m and rows >= n are zero; rows
+//              padded to a multiple of 128. A warp reading word w of its 32 vectors reads 512 contiguous bytes.
+//   LUT        per query group of Q queries, contiguous, already in the shared-memory layout of the scan:
+//              Q = 1: [s][c]; Q = 2: [s][c][2]; Q = 4: [s][c][4]; Q = 8: two [s][c][4] tables (queries 0-3, 4-7).
+//              One code byte then fetches all Q queries' entries with one LDS.32/64/128 (two LDS.128 for Q = 8).
+//   partials   [query][chunk][k] (dist, id) lists, merged by merge_kernel.
+#pragma once
+#include <cfloat>
+#include <cstdint>
+
+#include "vk_device.cuh"
+#include "warp_topk.cuh"
+
+namespace vk {
+
+// ------------------------------------------------------------------------------------------------ LUT builder
+// grid (m, groups), block 256: thread c computes centroid c of sub-space s for the Q queries of group g.
+// Arithmetic of the reference's l2sq (include/veckern/common.hpp:27-34): diff = q - c, acc += diff * diff in
+// j order, each operation rounded on its own (__fsub_rn / __fmul_rn / __fadd_rn: no FMA contraction).
+// Padded query slots (index >= nq) get 0.
+template <int Q>
+__global__ void __launch_bounds__(256) lut_kernel(const float* __restrict__ centroids,
+                                                  const float* __restrict__ queries, int64_t nq, int m, int dsub,
+                                                  float* __restrict__ lut) {
+    extern __shared__ float qsub[];  // [Q][dsub]
+    const int s = blockIdx.x, g = blockIdx.y, c = threadIdx.x;
+    const int64_t d = (int64_t)m * dsub;
+    for (int t = threadIdx.x; t < Q * dsub; t += blockDim.x) {
+        const int qq = t / dsub, j = t - qq * dsub;
+        const int64_t qi = (int64_t)g * Q + qq;
+        qsub[t] = qi < nq ? queries[qi * d + (int64_t)s * dsub + j] : 0.f;
+    }
+    __syncthreads();
+    const float* cen = centroids + ((int64_t)s * KSUB + c) * dsub;
+    float acc[Q];
+#pragma unroll
+    for (int qq = 0; qq < Q; ++qq) acc[qq] = 0.f;
+    for (int j = 0; j < dsub; ++j) {
+        const float cj = cen[j];
+#pragma unroll
+        for (int qq = 0; qq < Q; ++qq) {
+            const float diff = __fsub_rn(qsub[qq * dsub + j], cj);
+            acc[qq] = __fadd_rn(acc[qq], __fmul_rn(diff, diff));
+        }
+    }
+#pragma unroll
+    for (int qq = 0; qq < Q; ++qq)
+        if ((int64_t)g * Q + qq >= nq) acc[qq] = 0.f;
+    float* out = lut + (int64_t)g * Q * m * KSUB;
+    const int e = s * KSUB + c;
+    if constexpr (Q == 1) {
+        out[e] = acc[0];
+    } else if constexpr (Q == 2) {
+        reinterpret_cast<float2*>(out)[e] = make_float2(acc[0], acc[1]);
+    } else if constexpr (Q == 4) {
+        reinterpret_cast<float4*>(out)[e] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    } else {
+        reinterpret_cast<float4*>(out)[e] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        reinterpret_cast<float4*>(out)[m * KSUB + e] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ fused scan
+struct ScanArgs {
+    const uint4* codes;  // interleaved layout, n_pad rows
+    const float* lut;    // groups x (Q * m * 256), scan layout
+    int2* part;          // [nq][chunks][k] partial lists (dist bits, id)
+    int* work_counter;   // dynamic work-item counter, zero before launch
+    int* status;         // kernel status word (ERR_* bits)
+    int64_t n, n_pad;    // valid rows, padded rows (multiple of 128)
+    int64_t chunk_len;   // rows per chunk, a multiple of 32 * ILP
+    int64_t id_base;     // global id = id_base + row
+    int m, W, nq, groups, chunks, k, stages;
+    long long wait_budget;  // SM cycles a bounded wait may take
+};
+
+// Shared-memory plan of scan_kernel; host and device compute it with the same function.
+struct ScanSmem {
+    uint32_t lut, stage, scratch, bars, flags, total, tile_bytes, lut_bytes;
+};
+__host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp, int nw, int stages, int k) {
+    auto up = [](uint32_t x, uint32_t a) { return (x + a - 1) / a * a; };
+    ScanSmem p;
+    p.lut_bytes = (uint32_t)Q * m * KSUB * 4u;
+    p.tile_bytes = (uint32_t)ilp * W * 512u;
+    p.lut = 0;
+    p.stage = up(p.lut_bytes, 128);
+    p.scratch = up(p.stage + (uint32_t)nw * stages * p.tile_bytes, 128);
+    p.bars = up(p.scratch + (uint32_t)nw * k * 8u, 16);
+    p.flags = p.bars + (uint32_t)(nw * stages + 1) * 8u;
+    p.total = up(p.flags + 16, 128);
+    return p;
+}
+
+// One sub-space lookup for Q queries: acc[q] += LUT_q[s][c], rounded per add, in s order.
+template <int Q>
+__device__ __forceinline__ void lookup_add(const unsigned char* lut_smem, int mtab, int s, uint32_t c,
+                                           float* acc) {
+    const uint32_t e = (uint32_t)s * KSUB + c;
+    if constexpr (Q == 1) {
+        acc[0] = __fadd_rn(acc[0], reinterpret_cast<const float*>(lut_smem)[e]);
+    } else if constexpr (Q == 2) {
+        const float2 v = reinterpret_cast<const float2*>(lut_smem)[e];
+        acc[0] = __fadd_rn(acc[0], v.x);
+        acc[1] = __fadd_rn(acc[1], v.y);
+    } else if constexpr (Q == 4) {
+        const float4 v = reinterpret_cast<const float4*>(lut_smem)[e];
+        acc[0] = __fadd_rn(acc[0], v.x);
+        acc[1] = __fadd_rn(acc[1], v.y);
+        acc[2] = __fadd_rn(acc[2], v.z);
+        acc[3] = __fadd_rn(acc[3], v.w);
+    } else {
+        const float4 v = reinterpret_cast<const float4*>(lut_smem)[e];
+        const float4 u = reinterpret_cast<const float4*>(lut_smem)[(uint32_t)mtab * KSUB + e];
+        acc[0] = __fadd_rn(acc[0], v.x);
+        acc[1] = __fadd_rn(acc[1], v.y);
+        acc[2] = __fadd_rn(acc[2], v.z);
+        acc[3] = __fadd_rn(acc[3], v.w);
+        acc[4] = __fadd_rn(acc[4], u.x);
+        acc[5] = __fadd_rn(acc[5], u.y);
+        acc[6] = __fadd_rn(acc[6], u.z);
+        acc[7] = __fadd_rn(acc[7], u.w);
+    }
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int b) {
+    return b < 4 ? v.x : b < 8 ? v.y : b < 12 ? v.z : v.w;
+}
+
+// Persistent fused scan + top-k. Work item = (vector chunk, query group), handed out by an atomic counter in
+// chunk-major order, so the blocks running at one time share the same chunk of codes through L2.
+//   per item:  (group changed) TMA bulk copy of the group's Q LUTs into shared memory;
+//              each warp streams its 32*ILP-row tiles of the chunk through a private ring of `stages` shared
+//              buffers filled by TMA bulk copies (lane 0 issues, mbarrier per slot), computes Q distances per
+//              row with strictly ordered fp32 adds, and offers them to one WarpTopK per query;
+//              the NW warp lists of each query are merged in shared memory into the item's partial list.
+// MT: m when it is 16, 32 or 64 (fully unrolled sub-space loop), 0 for any other m.
+template <int Q, int MT, int ILP, int S, int NW>
+__global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int W_T = MT ? (MT + 15) / 16 : 0;
+    const int m = MT ? MT : a.m;
+    const int W = MT ? W_T : a.W;
+    const ScanSmem plan = scan_smem_plan(Q, m, W, ILP, NW, a.stages, a.k);
+    unsigned char* lut_smem = smem + plan.lut;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + plan.bars);
+    uint64_t* lut_bar = bars + NW * a.stages;
+    int* s_item = reinterpret_cast<int*>(smem + plan.flags);
+    int* s_abort = s_item + 1;
+    int2* scratch = reinterpret_cast<int2*>(smem + plan.scratch);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t* my_bars = bars + warp * a.stages;
+    unsigned char* my_stages = smem + plan.stage + (uint32_t)warp * a.stages * plan.tile_bytes;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NW * a.stages + 1; ++i) mbar_init(bars + i, 1);
+        *s_abort = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    const int items = a.groups * a.chunks;
+    const int64_t tile_rows = 32 * ILP;
+    uint32_t issued = 0, consumed = 0, lut_phase = 0;  // issued: lane 0 only
+    int cur_g = -1;
+
+    for (;;) {
+        if (threadIdx.x == 0) *s_item = atomicAdd(a.work_counter, 1);
+        __syncthreads();  // (A) previous item finished by every warp; the LUT may be replaced
+        const int item = *s_item;
+        if (item >= items || *s_abort) break;
+        const int chunk = item / a.groups, g = item - chunk * a.groups;
+
+        if (g != cur_g) {
+            if (threadIdx.x == 0) {
+                fence_proxy_async_smem();
+                const unsigned char* src =
+                    reinterpret_cast<const unsigned char*>(a.lut) + (int64_t)g * plan.lut_bytes;
+                mbar_arrive_expect_tx(lut_bar, plan.lut_bytes);
+                for (uint32_t off = 0; off < plan.lut_bytes; off += 32768u) {
+                    const uint32_t len = min(32768u, plan.lut_bytes - off);
+                    bulk_g2s(lut_smem + off, src + off, len, lut_bar);
+                }
+            }
+            // Vote, so that the warp's lanes take the same path even if only some of them ran out of time.
+            if (!__all_sync(FULL, mbar_wait_bounded(lut_bar, lut_phase, a.wait_budget))) {
+                if (lane == 0) atomicOr(a.status, ERR_WAIT_TIMEOUT);
+                *s_abort = 1;
+            }
+            lut_phase ^= 1u;
+            cur_g = g;
+        }
+
+        WarpTopK<S> top[Q];
+#pragma unroll
+        for (int q = 0; q < Q; ++q) top[q].init();
+
+        const int64_t t_begin = (int64_t)chunk * a.chunk_len / tile_rows;
+        const int64_t t_end = min((int64_t)(chunk + 1) * a.chunk_len, a.n_pad) / tile_rows;
+        const int64_t my_tiles = t_end - t_begin > warp ? (t_end - t_begin - warp + NW - 1) / NW : 0;
+
+        auto issue = [&](int64_t j) {  // lane 0: tile j of this warp into the next ring slot
+            const int64_t t = t_begin + warp + j * NW;
+            const uint32_t slot = issued % (uint32_t)a.stages;
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(my_bars + slot, plan.tile_bytes);
+            bulk_g2s(my_stages + slot * plan.tile_bytes, a.codes + t * tile_rows * W, plan.tile_bytes,
+                     my_bars + slot);
+            ++issued;
+        };
+        bool warp_abort = __any_sync(FULL, *s_abort != 0);
+        if (lane == 0 && !warp_abort)
+            for (int64_t j = 0; j < (my_tiles < a.stages ? my_tiles : (int64_t)a.stages); ++j) issue(j);
+        __syncwarp();
+        for (int64_t j = 0; j < my_tiles && !warp_abort; ++j) {
+            const uint32_t slot = consumed % (uint32_t)a.stages;
+            const uint32_t parity = (consumed / (uint32_t)a.stages) & 1u;
+            if (!__all_sync(FULL, mbar_wait_bounded(my_bars + slot, parity, a.wait_budget))) {
+                if (lane == 0) atomicOr(a.status, ERR_WAIT_TIMEOUT);
+                *s_abort = 1;
+                warp_abort = true;
+                break;
+            }
+            ++consumed;
+            const uint4* st = reinterpret_cast<const uint4*>(my_stages + slot * plan.tile_bytes);
+
+            float acc[ILP][Q];
+#pragma unroll
+            for (int u = 0; u < ILP; ++u)
+#pragma unroll
+                for (int q = 0; q < Q; ++q) acc[u][q] = 0.f;
+
+#pragma unroll
+            for (int w = 0; w < (MT ? W_T : 1); ++w) {
+                // generic m: a run-time loop over words; MT: the unrolled loop above with W_T words
+                for (int wr = 0; wr < (MT ? 1 : W); ++wr) {
+                    const int ww = MT ? w : wr;
+                    uint4 cv[ILP];
+#pragma unroll
+                    for (int u = 0; u < ILP; ++u) cv[u] = st[(u * W + ww) * 32 + lane];
+#pragma unroll
+                    for (int b = 0; b < 16; ++b) {
+                        const int s = ww * 16 + b;
+                        if (!MT && s >= m) break;
+#pragma unroll
+                        for (int u = 0; u < ILP; ++u) {
+                            const uint32_t c = (word_of(cv[u], b) >> (8 * (b & 3))) & 0xffu;
+                            lookup_add<Q>(lut_smem, m, s, c, acc[u]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();  // every lane has consumed the slot (the codes fed the lookups above)
+            if (lane == 0 && j + a.stages < my_tiles) issue(j + a.stages);
+
+            const int64_t t = t_begin + warp + j * NW;
+            bool any = false;
+            int32_t ids[ILP];
+            bool valid[ILP];
+#pragma unroll
+            for (int u = 0; u < ILP; ++u) {
+                const int64_t row = t * tile_rows + u * 32 + lane;
+                valid[u] = row < a.n;
+                ids[u] = (int32_t)(a.id_base + row);
+#pragma unroll
+                for (int q = 0; q < Q; ++q) any |= valid[u] && top[q].admits(acc[u][q], ids[u]);
+            }
+            if (__any_sync(FULL, any)) {
+#pragma unroll
+                for (int u = 0; u < ILP; ++u)
+#pragma unroll
+                    for (int q = 0; q < Q; ++q) top[q].offer(acc[u][q], ids[u], valid[u], a.k);
+            }
+        }
+        if (warp_abort && lane == 0) {
+            // Let this warp's copies still in flight land before the block can exit.
+            while (consumed < issued) {
+                const uint32_t slot = consumed % (uint32_t)a.stages;
+                mbar_wait_bounded(my_bars + slot, (consumed / (uint32_t)a.stages) & 1u, a.wait_budget);
+                ++consumed;
+            }
+        }
+        consumed = __shfl_sync(FULL, consumed, 0);
+
+        __syncthreads();  // (B) all warps finished the item's tiles; s_abort is stable
+        if (*s_abort) continue;  // uniform: the next (A) exits the loop
+        // Merge the NW warp lists of each query into the item's partial list.
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            const int64_t qi = (int64_t)g * Q + q;
+            if (qi < a.nq) {  // uniform
+                top[q].store(scratch + warp * a.k, a.k);
+                __syncthreads();
+                if (warp == 0) {
+                    WarpTopK<S> mt;
+                    mt.init();
+                    const int total = NW * a.k;
+                    for (int j0 = 0; j0 < total; j0 += 32) {
+                        const int j = j0 + lane;
+                        const int2 e = j < total ? scratch[j] : make_int2(0x7f800000, SENTINEL_ID);
+                        mt.offer(__int_as_float(e.x), e.y, j < total, a.k);
+                    }
+                    mt.store(a.part + (qi * a.chunks + chunk) * a.k, a.k);
+                }
+                __syncthreads();
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ merge
+// One warp per query: the k best of `lists` sorted lists of k_in entries (entry (q, l, j) at
+// in[q * qstride + l * lstride + j]); entries with id < 0 are padding. Output ascending, empty slots {+inf, -1}
+// (the reference's host fix-up, src/cuda/searcher.cu:514-517).
+template <int S>
+__global__ void __launch_bounds__(128) merge_kernel(const int2* __restrict__ in, int64_t nq, int lists, int k_in,
+                                                    int64_t qstride, int64_t lstride, int k,
+                                                    int2* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t q = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (q >= nq) return;  // warp-uniform
+    WarpTopK<S> top;
+    top.init();
+    const int64_t total = (int64_t)lists * k_in;
+    const int2* base = in + q * qstride;
+    for (int64_t j0 = 0; j0 < total; j0 += 32) {
+        const int64_t j = j0 + lane;
+        int2 e = make_int2(0x7f800000, SENTINEL_ID);
+        if (j < total) {
+            const int64_t l = j / k_in, i = j - l * k_in;
+            e = base[l * lstride + i];
+        }
+        top.offer(__int_as_float(e.x), e.y, j < total && e.y >= 0, k);
+    }
+#pragma unroll
+    for (int r = 0; r < S; ++r) {
+        const int e = r * 32 + lane;
+        if (e < k) {
+            const bool pad = top.id[r] == SENTINEL_ID;
+            out[q * k + e] = pad ? make_int2(0x7f800000, -1) : make_int2(__float_as_int(top.d[r]), top.id[r]);
+        }
+    }
+}
+
+}  // namespace vk

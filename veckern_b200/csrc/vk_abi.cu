@@ -1,0 +1,767 @@
+// VecKern-B200 C ABI implementation: index ownership, launch planning for the B200's 148 SMs, query batching,
+// per-stage CUDA-event timing, and the error convention (int status + vk_last_error).
+//
+// Reference behaviour this file reproduces (shivdeshpande/VecKern):
+//   PQSearcher ctor      src/cuda/searcher.cu:427-444   (copy centroids + codes to the device once)
+//   search               src/cuda/searcher.cu:466-520   (k in [1, min(128, n)], batches, stage timings)
+//   distances            src/cuda/searcher.cu:522-547   (nq x n matrix, 512 MB batches, unfused variants only)
+//   validation           src/cuda/searcher.cu:243-249, 450-460
+//   device_info          src/cuda/searcher.cu:143-156
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <limits>
+#include <string>
+
+#include "../../include/vk_abi.h"
+#include "aux_kernels.cuh"
+#include "kernels.cuh"
+#include "scan_dispatch.cuh"
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_error = buf;
+    return code;
+}
+
+#define VK_TRY_CUDA(call)                                                                                  \
+    do {                                                                                                   \
+        const cudaError_t e_ = (call);                                                                     \
+        if (e_ != cudaSuccess) return fail(e_ == cudaErrorMemoryAllocation ? VK_ERR_NOMEM : VK_ERR_CUDA, \
+                                           "%s failed: %s", #call, cudaGetErrorString(e_));                \
+    } while (0)
+
+#define VK_TRY(call)                    \
+    do {                                \
+        const int r_ = (call);          \
+        if (r_ != VK_OK) return r_;     \
+    } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    cudaError_t err = cudaSuccess;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) err = cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+template <typename T>
+struct DevBuf {
+    T* ptr = nullptr;
+    size_t cap = 0;  // elements
+    ~DevBuf() { release(); }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        cap = 0;
+    }
+    // Grows (never shrinks), like the reference's DeviceBuffer::ensure (src/cuda/searcher.cu:31-37).
+    int ensure(size_t count) {
+        if (count <= cap) return VK_OK;
+        release();
+        const cudaError_t e = cudaMalloc(&ptr, std::max<size_t>(count, 1) * sizeof(T));
+        if (e != cudaSuccess) {
+            ptr = nullptr;
+            return fail(VK_ERR_NOMEM, "cudaMalloc of %zu bytes failed: %s", count * sizeof(T), cudaGetErrorString(e));
+        }
+        cap = count;
+        return VK_OK;
+    }
+};
+
+constexpr int64_t kMaxRowsPerChunk = 1 << 20;       // L2 locality: a chunk's codes stay well inside the 126 MB L2
+constexpr size_t kLutBudgetBytes = size_t(1) << 30;  // LUT buffer cap per query batch
+constexpr size_t kDistanceBudgetBytes = size_t(512) << 20;  // distances(): the reference's 512 MB cap
+constexpr int kStagesMax = 4;
+
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+bool is_fused_variant(int v) { return v >= VK_VARIANT_FUSED && v <= VK_VARIANT_FUSED_WARP; }
+bool needs_m16(int v) {
+    return v == VK_VARIANT_SHARED_LUT_VEC || v == VK_VARIANT_FUSED_VEC || v == VK_VARIANT_FUSED_VEC_MQ ||
+           v == VK_VARIANT_FUSED_WARP;
+}
+const char* variant_name(int v) {
+    static const char* names[] = {"v0_global_lut", "v1_shared_lut", "v2_shared_lut_vec", "v3_interleaved",
+                                  "v4_fused",      "v5_fused_reg",  "v6_fused_vec",      "v7_fused_vec_mq",
+                                  "v8_fused_warp"};
+    return v >= 0 && v <= 8 ? names[v] : "unknown";
+}
+
+const void* scan_kernel_ptr(int Q, int mt, int ilp, int s) {
+    switch (Q) {
+        case 1: return vk::scan_kernel_for<1>(mt, ilp, s);
+        case 2: return vk::scan_kernel_for<2>(mt, ilp, s);
+        case 4: return vk::scan_kernel_for<4>(mt, ilp, s);
+        case 8: return vk::scan_kernel_for<8>(mt, ilp, s);
+        default: return nullptr;
+    }
+}
+
+const void* lut_kernel_ptr(int Q) {
+    switch (Q) {
+        case 1: return reinterpret_cast<const void*>(&vk::lut_kernel<1>);
+        case 2: return reinterpret_cast<const void*>(&vk::lut_kernel<2>);
+        case 4: return reinterpret_cast<const void*>(&vk::lut_kernel<4>);
+        default: return reinterpret_cast<const void*>(&vk::lut_kernel<8>);
+    }
+}
+
+const void* merge_kernel_ptr(int s) {
+    switch (s) {
+        case 1: return reinterpret_cast<const void*>(&vk::merge_kernel<1>);
+        case 2: return reinterpret_cast<const void*>(&vk::merge_kernel<2>);
+        default: return reinterpret_cast<const void*>(&vk::merge_kernel<4>);
+    }
+}
+
+int s_for_k(int k) { return k <= 32 ? 1 : k <= 64 ? 2 : 4; }
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------ index
+struct vk_index {
+    int device = 0;
+    int m = 0, dsub = 0, W = 0;
+    int64_t n = 0, n_pad = 0, id_base = 0;
+    float* centroids = nullptr;
+    uint4* codes = nullptr;
+    cudaStream_t stream = nullptr;
+    DevBuf<float> queries, lut, dists;
+    DevBuf<int2> part, out;
+    int* flags = nullptr;  // [0] work counter, [1] kernel status word
+    cudaEvent_t ev[6] = {};
+    int sm_count = 0, smem_optin = 0, clock_khz = 0;
+    long long wait_budget = 0;
+
+    ~vk_index() {
+        DeviceGuard g(device);
+        for (auto& e : ev)
+            if (e) cudaEventDestroy(e);
+        if (stream) cudaStreamDestroy(stream);
+        if (centroids) cudaFree(centroids);
+        if (codes) cudaFree(codes);
+        if (flags) cudaFree(flags);
+    }
+};
+
+namespace {
+
+struct Plan {
+    int Q = 1, ilp = 1, stages = kStagesMax, S = 1, mt = 0;
+    int threads = 0, blocks_per_sm = 0, grid = 0;
+    int groups = 0, chunks = 0;
+    int64_t chunk_len = 0;
+    uint32_t smem = 0;
+    const void* fn = nullptr;
+};
+
+// Chooses Q (the requested queries per block, halved until the LUTs fit, and never more than the batch needs),
+// ILP and the ring depth, then the chunk count with a wave model over the occupancy API's resident blocks:
+// time ~ ceil(items / resident) * (rows per chunk + a LUT-load overhead), minimised over the chunk count.
+int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan& p) {
+    const int nw = vk::kScanWarps;
+    p.threads = nw * 32;
+    p.S = s_for_k(k);
+    p.mt = (ix->m == 16 || ix->m == 32 || ix->m == 64) ? ix->m : 0;
+    int Q = t.queries_per_block;
+    int64_t need = 1;
+    while (need < nq && need < 8) need *= 2;
+    Q = (int)std::min<int64_t>(Q, need);
+    p.ilp = t.vectors_per_step;
+    p.stages = kStagesMax;
+    auto fits = [&](int q, int ilp, int st) {
+        return vk::scan_smem_plan(q, ix->m, ix->W, ilp, nw, st, k).total <= (uint32_t)ix->smem_optin;
+    };
+    for (;;) {
+        if (fits(Q, p.ilp, p.stages)) break;
+        if (p.stages > 2) { --p.stages; continue; }
+        if (p.ilp > 1) { p.ilp /= 2; p.stages = kStagesMax; continue; }
+        if (Q > 1) { Q /= 2; p.ilp = t.vectors_per_step; p.stages = kStagesMax; continue; }
+        return fail(VK_ERR_INVALID, "LUT does not fit in shared memory (m = %d needs %u bytes, device allows %d)",
+                    ix->m, vk::scan_smem_plan(1, ix->m, ix->W, 1, nw, 2, k).total, ix->smem_optin);
+    }
+    p.Q = Q;
+    p.fn = scan_kernel_ptr(Q, p.mt, p.ilp, p.S);
+    if (!p.fn) return fail(VK_ERR_UNSUPPORTED, "no scan kernel for Q=%d m=%d ilp=%d", Q, ix->m, p.ilp);
+    p.smem = vk::scan_smem_plan(Q, ix->m, ix->W, p.ilp, nw, p.stages, k).total;
+    VK_TRY_CUDA(cudaFuncSetAttribute(p.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+    int per_sm = 0;
+    VK_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, p.fn, p.threads, p.smem));
+    p.blocks_per_sm = std::max(per_sm, 1);
+    const int64_t resident = (int64_t)p.blocks_per_sm * ix->sm_count;
+
+    p.groups = (int)ceil_div(nq, Q);
+    const int64_t tile_rows = 32 * p.ilp;
+    const int64_t tiles = ix->n_pad / tile_rows;
+    const int64_t max_chunks = std::max<int64_t>(1, tiles / (2 * nw));  // >= 2 tiles per warp per chunk
+    const int64_t min_chunks = std::min(max_chunks, ceil_div(ix->n_pad, kMaxRowsPerChunk));
+    int64_t chunks = min_chunks;
+    if (t.blocks_per_query > 0) {
+        chunks = std::min<int64_t>(t.blocks_per_query, max_chunks);
+    } else {
+        const double lut_rows = 512.0;  // LUT reload per item, in rows of scan work
+        double best = 1e300;
+        const int64_t hi = std::min(max_chunks, min_chunks + 8 * resident);
+        for (int64_t c = min_chunks; c <= hi; ++c) {
+            const double waves = (double)ceil_div((int64_t)p.groups * c, resident);
+            const double cost = waves * ((double)ix->n_pad / c + lut_rows);
+            if (cost < best * 0.999) {
+                best = cost;
+                chunks = c;
+            }
+        }
+    }
+    p.chunk_len = ceil_div(tiles, chunks) * tile_rows;
+    p.chunks = (int)ceil_div(ix->n_pad, p.chunk_len);
+    const int64_t items = (int64_t)p.groups * p.chunks;
+    if (items > std::numeric_limits<int>::max() / 2)
+        return fail(VK_ERR_UNSUPPORTED, "too many work items (%lld); search fewer queries per call", (long long)items);
+    p.grid = (int)std::min<int64_t>(items, resident);
+    return VK_OK;
+}
+
+int validate_tuning(const vk_tuning_t* t) {
+    if (!t) return VK_OK;
+    if (!(t->scan_threads >= 32 && t->scan_threads <= 1024 && t->scan_threads % 32 == 0))
+        return fail(VK_ERR_INVALID, "scan_threads must be a multiple of 32 in [32, 1024]");
+    if (t->blocks_per_query < 0) return fail(VK_ERR_INVALID, "blocks_per_query must be >= 0");
+    if (!(t->queries_per_block == 1 || t->queries_per_block == 2 || t->queries_per_block == 4 ||
+          t->queries_per_block == 8))
+        return fail(VK_ERR_INVALID, "queries_per_block must be 1, 2, 4 or 8");
+    if (!(t->vectors_per_step == 1 || t->vectors_per_step == 2 || t->vectors_per_step == 4))
+        return fail(VK_ERR_INVALID, "vectors_per_step must be 1, 2 or 4");
+    return VK_OK;
+}
+
+int check_variant(const vk_index* ix, int variant) {
+    if (variant < 0 || variant > 8) return fail(VK_ERR_INVALID, "unknown scan variant %d", variant);
+    if (needs_m16(variant) && ix->m % 16 != 0)
+        return fail(VK_ERR_INVALID, "%s requires m %% 16 == 0", variant_name(variant));
+    if ((int64_t)ix->m * vk::KSUB * 4 > ix->smem_optin)
+        return fail(VK_ERR_INVALID, "LUT does not fit in shared memory");
+    return VK_OK;
+}
+
+// Launches LUT -> scan -> merge for one batch of device-resident queries into d_out (nq x k).
+int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk_tuning_t& t, int2* d_out,
+               cudaStream_t st, vk_launch_shape_t* shape, cudaEvent_t* marks) {
+    Plan p;
+    VK_TRY(plan_scan(ix, nq, k, t, p));
+    const int64_t lut_floats = (int64_t)p.groups * p.Q * ix->m * vk::KSUB;
+    VK_TRY(ix->lut.ensure(lut_floats));
+    VK_TRY(ix->part.ensure((size_t)nq * p.chunks * k));
+
+    // LUT
+    {
+        const void* fn = lut_kernel_ptr(p.Q);
+        const size_t smem = (size_t)p.Q * ix->dsub * sizeof(float);
+        if (smem > 48 * 1024) VK_TRY_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        const float* cen = ix->centroids;
+        float* lut = ix->lut.ptr;
+        int m = ix->m, dsub = ix->dsub;
+        void* args[] = {(void*)&cen, (void*)&d_queries, (void*)&nq, (void*)&m, (void*)&dsub, (void*)&lut};
+        VK_TRY_CUDA(cudaLaunchKernel(fn, dim3(ix->m, p.groups), dim3(vk::KSUB), args, smem, st));
+    }
+    if (marks) VK_TRY_CUDA(cudaEventRecord(marks[0], st));
+    // fused scan + top-k
+    {
+        VK_TRY_CUDA(cudaMemsetAsync(ix->flags, 0, sizeof(int), st));
+        vk::ScanArgs a{};
+        a.codes = ix->codes;
+        a.lut = ix->lut.ptr;
+        a.part = ix->part.ptr;
+        a.work_counter = ix->flags;
+        a.status = ix->flags + 1;
+        a.n = ix->n;
+        a.n_pad = ix->n_pad;
+        a.chunk_len = p.chunk_len;
+        a.id_base = ix->id_base;
+        a.m = ix->m;
+        a.W = ix->W;
+        a.nq = (int)nq;
+        a.groups = p.groups;
+        a.chunks = p.chunks;
+        a.k = k;
+        a.stages = p.stages;
+        a.wait_budget = ix->wait_budget;
+        void* args[] = {(void*)&a};
+        VK_TRY_CUDA(cudaLaunchKernel(p.fn, dim3(p.grid), dim3(p.threads), args, p.smem, st));
+    }
+    if (marks) VK_TRY_CUDA(cudaEventRecord(marks[1], st));
+    // merge of the per-chunk partial lists
+    {
+        const void* fn = merge_kernel_ptr(p.S);
+        const int2* in = ix->part.ptr;
+        int lists = p.chunks, k_in = k, kk = k;
+        int64_t qstride = (int64_t)p.chunks * k, lstride = k;
+        void* args[] = {(void*)&in, (void*)&nq, (void*)&lists, (void*)&k_in, (void*)&qstride, (void*)&lstride,
+                        (void*)&kk, (void*)&d_out};
+        VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)ceil_div(nq, 4)), dim3(128), args, 0, st));
+    }
+    if (shape) {
+        shape->threads = p.threads;
+        shape->blocks_x = p.chunks;
+        shape->grid_y = p.groups;
+        shape->queries_per_block = p.Q;
+        shape->vectors_per_step = p.ilp;
+        shape->blocks_per_sm = p.blocks_per_sm;
+        shape->waves = (double)p.groups * p.chunks / ((double)p.blocks_per_sm * ix->sm_count);
+    }
+    return VK_OK;
+}
+
+int read_status(vk_index* ix, cudaStream_t st) {
+    int status = 0;
+    VK_TRY_CUDA(cudaMemcpyAsync(&status, ix->flags + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
+    VK_TRY_CUDA(cudaStreamSynchronize(st));
+    if (status != 0) {
+        VK_TRY_CUDA(cudaMemsetAsync(ix->flags + 1, 0, sizeof(int), st));
+        VK_TRY_CUDA(cudaStreamSynchronize(st));
+        return fail(VK_ERR_DEVICE, "kernel reported status 0x%x (a bounded wait ran out)", status);
+    }
+    return VK_OK;
+}
+
+int64_t max_query_batch(const vk_index* ix) {
+    // grid.y of the LUT and distance kernels stays below 65536 and the LUT buffer within its budget
+    const int64_t by_lut = std::max<int64_t>(8, (int64_t)(kLutBudgetBytes / ((size_t)ix->m * vk::KSUB * 4)));
+    return std::min<int64_t>(by_lut, 65528) / 8 * 8;
+}
+
+int create_common(int device, const float* centroids, int m, int dsub, int64_t n, int64_t id_base,
+                  vk_index** out, vk_index*& ix) {
+    if (!out) return fail(VK_ERR_INVALID, "out must not be NULL");
+    *out = nullptr;
+    if (!centroids) return fail(VK_ERR_INVALID, "centroids must not be NULL");
+    if (m <= 0 || dsub <= 0) return fail(VK_ERR_INVALID, "m and dsub must be positive");
+    if (n <= 0 || n >= (int64_t)std::numeric_limits<int>::max())
+        return fail(VK_ERR_INVALID, "n must fit in int32 ids");
+    if (id_base < 0 || id_base + n > (int64_t)std::numeric_limits<int>::max())
+        return fail(VK_ERR_INVALID, "id_base + n must fit in int32 ids");
+    int count = 0;
+    VK_TRY_CUDA(cudaGetDeviceCount(&count));
+    if (device < 0 || device >= count) return fail(VK_ERR_INVALID, "device %d does not exist", device);
+    ix = new vk_index();
+    ix->device = device;
+    ix->m = m;
+    ix->dsub = dsub;
+    ix->W = (m + 15) / 16;
+    ix->n = n;
+    ix->n_pad = ceil_div(n, 128) * 128;
+    ix->id_base = id_base;
+    VK_TRY_CUDA(cudaDeviceGetAttribute(&ix->sm_count, cudaDevAttrMultiProcessorCount, device));
+    VK_TRY_CUDA(cudaDeviceGetAttribute(&ix->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    VK_TRY_CUDA(cudaDeviceGetAttribute(&ix->clock_khz, cudaDevAttrClockRate, device));
+    ix->wait_budget = (long long)std::max(ix->clock_khz, 1000000) * 1000LL * 2;  // about two seconds
+    VK_TRY_CUDA(cudaStreamCreateWithFlags(&ix->stream, cudaStreamNonBlocking));
+    for (auto& e : ix->ev) VK_TRY_CUDA(cudaEventCreate(&e));
+    VK_TRY_CUDA(cudaMalloc(&ix->flags, 4 * sizeof(int)));
+    VK_TRY_CUDA(cudaMemsetAsync(ix->flags, 0, 4 * sizeof(int), ix->stream));
+    const size_t cbytes = (size_t)m * vk::KSUB * dsub * sizeof(float);
+    VK_TRY_CUDA(cudaMalloc(&ix->centroids, cbytes));
+    VK_TRY_CUDA(cudaMemcpyAsync(ix->centroids, centroids, cbytes, cudaMemcpyHostToDevice, ix->stream));
+    VK_TRY_CUDA(cudaMalloc(&ix->codes, (size_t)ix->n_pad * ix->W * sizeof(uint4)));
+    VK_TRY_CUDA(cudaMemsetAsync(ix->codes, 0, (size_t)ix->n_pad * ix->W * sizeof(uint4), ix->stream));
+    return VK_OK;
+}
+
+unsigned grid_for(int64_t total, int sm_count) {
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), (int64_t)sm_count * 16));
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------ C ABI
+extern "C" {
+
+size_t vk_last_error(char* buf, size_t len) {
+    if (buf && len > 0) {
+        const size_t n = std::min(len - 1, g_error.size());
+        std::memcpy(buf, g_error.data(), n);
+        buf[n] = '\0';
+    }
+    return g_error.size();
+}
+
+void vk_tuning_default(vk_tuning_t* t) {
+    if (!t) return;
+    t->scan_threads = 256;
+    t->blocks_per_query = 0;
+    t->queries_per_block = 2;
+    t->vectors_per_step = 4;
+}
+
+int vk_tuning_validate(const vk_tuning_t* t) {
+    if (!t) return fail(VK_ERR_INVALID, "tuning must not be NULL");
+    return validate_tuning(t);
+}
+
+int vk_device_info(int device, vk_device_info_t* out) {
+    if (!out) return fail(VK_ERR_INVALID, "out must not be NULL");
+    cudaDeviceProp prop{};
+    VK_TRY_CUDA(cudaGetDeviceProperties(&prop, device));
+    std::memset(out, 0, sizeof(*out));
+    std::snprintf(out->name, sizeof(out->name), "%s", prop.name);
+    int mem_khz = 0, bus = 0, smem = 0, clk = 0;
+    VK_TRY_CUDA(cudaDeviceGetAttribute(&out->sm_count, cudaDevAttrMultiProcessorCount, device));
+    VK_TRY_CUDA(cudaDeviceGetAttribute(&mem_khz, cudaDevAttrMemoryClockRate, device));
+    VK_TRY_CUDA(cudaDeviceGetAttribute(&bus, cudaDevAttrGlobalMemoryBusWidth, device));
+    VK_TRY_CUDA(cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    VK_TRY_CUDA(cudaDeviceGetAttribute(&clk, cudaDevAttrClockRate, device));
+    out->peak_bandwidth_gbs = 2.0 * mem_khz * 1e3 * (bus / 8.0) / 1e9;
+    out->max_smem_per_block = (size_t)smem;
+    out->clock_mhz = clk / 1000;
+    return VK_OK;
+}
+
+int vk_index_create(int device, const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
+                    int64_t id_base, vk_index_t** out) {
+    if (!codes) return fail(VK_ERR_INVALID, "codes must not be NULL");
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(guard.err));
+    vk_index* ix = nullptr;
+    int rc = create_common(device, centroids, m, dsub, n, id_base, out, ix);
+    if (rc == VK_OK) {
+        // Upload row-major codes in slices through one staging buffer and interleave each slice on the device.
+        const int64_t slice = std::min<int64_t>(ceil_div(n, 32) * 32, int64_t(1) << 22);
+        uint8_t* staging = nullptr;
+        cudaError_t e = cudaMalloc(&staging, (size_t)slice * m);
+        for (int64_t r0 = 0; e == cudaSuccess && r0 < n; r0 += slice) {
+            const int64_t cnt = std::min(slice, n - r0);
+            e = cudaMemcpyAsync(staging, codes + r0 * m, (size_t)cnt * m, cudaMemcpyHostToDevice, ix->stream);
+            if (e == cudaSuccess) {
+                vk::interleave_kernel<<<grid_for(ceil_div(cnt, 32) * 32 * ix->W, ix->sm_count), 256, 0, ix->stream>>>(
+                    staging, r0, cnt, n, m, ix->W, ix->codes);
+                e = cudaGetLastError();
+            }
+            if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);  // staging is reused
+        }
+        if (staging) cudaFree(staging);
+        if (e != cudaSuccess) rc = fail(VK_ERR_CUDA, "code upload failed: %s", cudaGetErrorString(e));
+    }
+    if (rc == VK_OK) {
+        const cudaError_t e = cudaStreamSynchronize(ix->stream);
+        if (e != cudaSuccess) rc = fail(VK_ERR_CUDA, "index build failed: %s", cudaGetErrorString(e));
+    }
+    if (rc != VK_OK) {
+        delete ix;
+        return rc;
+    }
+    *out = ix;
+    return VK_OK;
+}
+
+int vk_index_create_from_device(int device, const float* centroids, int m, int dsub, const uint8_t* d_codes,
+                                int64_t n, int64_t id_base, vk_index_t** out) {
+    if (!d_codes) return fail(VK_ERR_INVALID, "codes must not be NULL");
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(guard.err));
+    vk_index* ix = nullptr;
+    int rc = create_common(device, centroids, m, dsub, n, id_base, out, ix);
+    if (rc == VK_OK) {
+        vk::interleave_kernel<<<grid_for(ix->n_pad * ix->W, ix->sm_count), 256, 0, ix->stream>>>(d_codes, 0, n, n, m,
+                                                                                                   ix->W, ix->codes);
+        cudaError_t e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);
+        if (e != cudaSuccess) rc = fail(VK_ERR_CUDA, "index build failed: %s", cudaGetErrorString(e));
+    }
+    if (rc != VK_OK) {
+        delete ix;
+        return rc;
+    }
+    *out = ix;
+    return VK_OK;
+}
+
+int vk_index_create_generated(int device, const float* centroids, int m, int dsub, uint64_t seed,
+                              const uint32_t* cdf, int clusters, int64_t row_first, int64_t n, int64_t id_base,
+                              vk_index_t** out) {
+    if (!cdf || clusters <= 0) return fail(VK_ERR_INVALID, "cdf must not be NULL and clusters must be positive");
+    if (row_first < 0) return fail(VK_ERR_INVALID, "row_first must be >= 0");
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(guard.err));
+    vk_index* ix = nullptr;
+    int rc = create_common(device, centroids, m, dsub, n, id_base, out, ix);
+    if (rc == VK_OK) {
+        uint32_t* d_cdf = nullptr;
+        const size_t bytes = (size_t)clusters * m * vk::KSUB * sizeof(uint32_t);
+        cudaError_t e = cudaMalloc(&d_cdf, bytes);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(d_cdf, cdf, bytes, cudaMemcpyHostToDevice, ix->stream);
+        if (e == cudaSuccess) {
+            vk::gen_interleaved_kernel<<<grid_for(ix->n_pad * ix->W, ix->sm_count), 256, 0, ix->stream>>>(
+                vk::mix64(seed), d_cdf, clusters, m, ix->W, row_first, n, ix->n_pad, ix->codes);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);
+        if (d_cdf) cudaFree(d_cdf);
+        if (e != cudaSuccess) rc = fail(VK_ERR_CUDA, "code generation failed: %s", cudaGetErrorString(e));
+    }
+    if (rc != VK_OK) {
+        delete ix;
+        return rc;
+    }
+    *out = ix;
+    return VK_OK;
+}
+
+int vk_index_destroy(vk_index_t* index) {
+    delete index;
+    return VK_OK;
+}
+
+int vk_index_info(const vk_index_t* ix, int64_t* n, int* m, int* dsub, int64_t* id_base, int* device) {
+    if (!ix) return fail(VK_ERR_INVALID, "index must not be NULL");
+    if (n) *n = ix->n;
+    if (m) *m = ix->m;
+    if (dsub) *dsub = ix->dsub;
+    if (id_base) *id_base = ix->id_base;
+    if (device) *device = ix->device;
+    return VK_OK;
+}
+
+int vk_index_get_codes(const vk_index_t* ix, int64_t first, int64_t count, uint8_t* out) {
+    if (!ix || !out) return fail(VK_ERR_INVALID, "index and out must not be NULL");
+    if (first < 0 || count < 0 || first + count > ix->n) return fail(VK_ERR_INVALID, "row range out of bounds");
+    if (count == 0) return VK_OK;
+    DeviceGuard guard(ix->device);
+    uint8_t* d = nullptr;
+    VK_TRY_CUDA(cudaMalloc(&d, (size_t)count * ix->m));
+    vk::deinterleave_kernel<<<grid_for(count * ix->m, ix->sm_count), 256, 0, ix->stream>>>(ix->codes, first, count,
+                                                                                           ix->m, ix->W, d);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, d, (size_t)count * ix->m, cudaMemcpyDeviceToHost, ix->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);
+    cudaFree(d);
+    if (e != cudaSuccess) return fail(VK_ERR_CUDA, "reading codes failed: %s", cudaGetErrorString(e));
+    return VK_OK;
+}
+
+int vk_search(vk_index_t* ix, const float* queries, int64_t nq, int k, int variant, const vk_tuning_t* tuning,
+              vk_neighbor_t* out, vk_timings_t* timings, vk_launch_shape_t* shape) {
+    if (!ix) return fail(VK_ERR_INVALID, "index must not be NULL");
+    if (k < 1 || k > 128 || (int64_t)k > ix->n) return fail(VK_ERR_INVALID, "k must be in [1, min(128, n)]");
+    if (nq < 0) return fail(VK_ERR_INVALID, "nq must be >= 0");
+    if (nq > 0 && (!queries || !out)) return fail(VK_ERR_INVALID, "queries and out must not be NULL");
+    VK_TRY(check_variant(ix, variant));
+    vk_tuning_t t;
+    vk_tuning_default(&t);
+    if (tuning) t = *tuning;
+    VK_TRY(validate_tuning(&t));
+    if (timings) *timings = vk_timings_t{};
+    if (nq == 0) return VK_OK;
+    DeviceGuard guard(ix->device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
+    cudaStream_t st = ix->stream;
+    const int64_t d = (int64_t)ix->m * ix->dsub;
+    const int64_t batch = std::min(nq, max_query_batch(ix));
+    VK_TRY(ix->queries.ensure((size_t)batch * d));
+    VK_TRY(ix->out.ensure((size_t)batch * k));
+    vk_timings_t acc{};
+    for (int64_t q0 = 0; q0 < nq; q0 += batch) {
+        const int64_t b = std::min(batch, nq - q0);
+        cudaEvent_t* ev = ix->ev;
+        VK_TRY_CUDA(cudaEventRecord(ev[0], st));
+        VK_TRY_CUDA(cudaMemcpyAsync(ix->queries.ptr, queries + q0 * d, (size_t)b * d * sizeof(float),
+                                    cudaMemcpyHostToDevice, st));
+        VK_TRY_CUDA(cudaEventRecord(ev[1], st));
+        cudaEvent_t marks[2] = {ev[2], ev[3]};
+        VK_TRY(run_search(ix, ix->queries.ptr, b, k, t, ix->out.ptr, st, shape, marks));
+        VK_TRY_CUDA(cudaEventRecord(ev[4], st));
+        VK_TRY_CUDA(cudaMemcpyAsync(out + q0 * k, ix->out.ptr, (size_t)b * k * sizeof(int2), cudaMemcpyDeviceToHost,
+                                    st));
+        VK_TRY_CUDA(cudaEventRecord(ev[5], st));
+        VK_TRY_CUDA(cudaEventSynchronize(ev[5]));
+        float ms[5];
+        for (int i = 0; i < 5; ++i) VK_TRY_CUDA(cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]));
+        acc.transfer_ms += ms[0] + ms[4];
+        acc.lut_ms += ms[1];
+        acc.scan_ms += ms[2];
+        acc.select_ms += ms[3];
+    }
+    VK_TRY(read_status(ix, st));
+    if (timings) *timings = acc;
+    return VK_OK;
+}
+
+int vk_search_device(vk_index_t* ix, const float* d_queries, int64_t nq, int k, const vk_tuning_t* tuning,
+                     vk_neighbor_t* d_out, void* stream) {
+    if (!ix) return fail(VK_ERR_INVALID, "index must not be NULL");
+    if (k < 1 || k > 128 || (int64_t)k > ix->n) return fail(VK_ERR_INVALID, "k must be in [1, min(128, n)]");
+    if (nq < 0) return fail(VK_ERR_INVALID, "nq must be >= 0");
+    if (nq > 0 && (!d_queries || !d_out)) return fail(VK_ERR_INVALID, "queries and out must not be NULL");
+    if (nq > max_query_batch(ix))
+        return fail(VK_ERR_INVALID, "nq %lld exceeds the device-path batch limit %lld", (long long)nq,
+                    (long long)max_query_batch(ix));
+    vk_tuning_t t;
+    vk_tuning_default(&t);
+    if (tuning) t = *tuning;
+    VK_TRY(validate_tuning(&t));
+    if (nq == 0) return VK_OK;
+    DeviceGuard guard(ix->device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ix->stream;
+    return run_search(ix, d_queries, nq, k, t, reinterpret_cast<int2*>(d_out), st, nullptr, nullptr);
+}
+
+int vk_index_sync(vk_index_t* ix, void* stream) {
+    if (!ix) return fail(VK_ERR_INVALID, "index must not be NULL");
+    DeviceGuard guard(ix->device);
+    return read_status(ix, stream ? static_cast<cudaStream_t>(stream) : ix->stream);
+}
+
+int vk_distances(vk_index_t* ix, const float* queries, int64_t nq, int variant, const vk_tuning_t* tuning,
+                 float* out, vk_timings_t* timings) {
+    if (!ix) return fail(VK_ERR_INVALID, "index must not be NULL");
+    if (variant < 0 || variant > 8) return fail(VK_ERR_INVALID, "unknown scan variant %d", variant);
+    if (is_fused_variant(variant)) return fail(VK_ERR_INVALID, "fused variants do not materialise distances");
+    VK_TRY(check_variant(ix, variant));
+    vk_tuning_t t;
+    vk_tuning_default(&t);
+    if (tuning) t = *tuning;
+    VK_TRY(validate_tuning(&t));
+    if (timings) *timings = vk_timings_t{};
+    if (nq < 0) return fail(VK_ERR_INVALID, "nq must be >= 0");
+    if (nq == 0) return VK_OK;
+    if (!queries || !out) return fail(VK_ERR_INVALID, "queries and out must not be NULL");
+    DeviceGuard guard(ix->device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
+    cudaStream_t st = ix->stream;
+    const int64_t d = (int64_t)ix->m * ix->dsub;
+    const int64_t batch =
+        std::max<int64_t>(1, std::min<int64_t>(65535, (int64_t)(kDistanceBudgetBytes / ((size_t)ix->n * 4))));
+    const int64_t b0 = std::min(batch, nq);
+    VK_TRY(ix->queries.ensure((size_t)b0 * d));
+    VK_TRY(ix->lut.ensure((size_t)b0 * ix->m * vk::KSUB));
+    VK_TRY(ix->dists.ensure((size_t)b0 * ix->n));
+    const size_t lut_smem = (size_t)ix->m * vk::KSUB * sizeof(float);
+    VK_TRY_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(&vk::dist_kernel),
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lut_smem));
+    vk_timings_t acc{};
+    cudaEvent_t* ev = ix->ev;
+    for (int64_t q0 = 0; q0 < nq; q0 += batch) {
+        const int64_t b = std::min(batch, nq - q0);
+        VK_TRY_CUDA(cudaEventRecord(ev[0], st));
+        VK_TRY_CUDA(cudaMemcpyAsync(ix->queries.ptr, queries + q0 * d, (size_t)b * d * sizeof(float),
+                                    cudaMemcpyHostToDevice, st));
+        VK_TRY_CUDA(cudaEventRecord(ev[1], st));
+        vk::lut_kernel<1><<<dim3(ix->m, (unsigned)b), vk::KSUB, ix->dsub * sizeof(float), st>>>(
+            ix->centroids, ix->queries.ptr, b, ix->m, ix->dsub, ix->lut.ptr);
+        VK_TRY_CUDA(cudaGetLastError());
+        VK_TRY_CUDA(cudaEventRecord(ev[2], st));
+        const int threads = t.scan_threads;
+        const int64_t bx = std::max<int64_t>(1, std::min<int64_t>(ceil_div(ix->n, threads),
+                                                                  ceil_div(8LL * ix->sm_count, b)));
+        vk::dist_kernel<<<dim3((unsigned)bx, (unsigned)b), threads, lut_smem, st>>>(ix->codes, ix->lut.ptr, ix->n,
+                                                                                    ix->m, ix->W, ix->dists.ptr);
+        VK_TRY_CUDA(cudaGetLastError());
+        VK_TRY_CUDA(cudaEventRecord(ev[3], st));
+        VK_TRY_CUDA(cudaMemcpyAsync(out + q0 * ix->n, ix->dists.ptr, (size_t)b * ix->n * sizeof(float),
+                                    cudaMemcpyDeviceToHost, st));
+        VK_TRY_CUDA(cudaEventRecord(ev[4], st));
+        VK_TRY_CUDA(cudaEventSynchronize(ev[4]));
+        float ms[4];
+        for (int i = 0; i < 4; ++i) VK_TRY_CUDA(cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]));
+        acc.transfer_ms += ms[0] + ms[3];
+        acc.lut_ms += ms[1];
+        acc.scan_ms += ms[2];
+    }
+    if (timings) *timings = acc;
+    return VK_OK;
+}
+
+int vk_compute_lut_device(vk_index_t* ix, const float* d_queries, int64_t nq, float* d_lut, void* stream) {
+    if (!ix) return fail(VK_ERR_INVALID, "index must not be NULL");
+    if (nq < 0) return fail(VK_ERR_INVALID, "nq must be >= 0");
+    if (nq == 0) return VK_OK;
+    if (!d_queries || !d_lut) return fail(VK_ERR_INVALID, "queries and lut must not be NULL");
+    if (nq > 65535) return fail(VK_ERR_INVALID, "at most 65535 queries per call");
+    DeviceGuard guard(ix->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ix->stream;
+    vk::lut_kernel<1><<<dim3(ix->m, (unsigned)nq), vk::KSUB, ix->dsub * sizeof(float), st>>>(ix->centroids, d_queries,
+                                                                                             nq, ix->m, ix->dsub, d_lut);
+    VK_TRY_CUDA(cudaGetLastError());
+    return VK_OK;
+}
+
+int vk_merge_topk_device(int device, const vk_neighbor_t* d_in, int64_t nq, int lists, int k_in,
+                         int64_t query_stride, int64_t list_stride, int k, vk_neighbor_t* d_out, void* stream) {
+    if (k < 1 || k > 128) return fail(VK_ERR_INVALID, "k must be in [1, 128]");
+    if (nq < 0 || lists < 0 || k_in < 0) return fail(VK_ERR_INVALID, "sizes must be >= 0");
+    if (nq == 0) return VK_OK;
+    if (!d_in || !d_out) return fail(VK_ERR_INVALID, "in and out must not be NULL");
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int2* in = reinterpret_cast<const int2*>(d_in);
+    int2* o = reinterpret_cast<int2*>(d_out);
+    switch (s_for_k(k)) {
+        case 1: vk::merge_kernel<1><<<(unsigned)ceil_div(nq, 4), 128, 0, st>>>(in, nq, lists, k_in, query_stride, list_stride, k, o); break;
+        case 2: vk::merge_kernel<2><<<(unsigned)ceil_div(nq, 4), 128, 0, st>>>(in, nq, lists, k_in, query_stride, list_stride, k, o); break;
+        default: vk::merge_kernel<4><<<(unsigned)ceil_div(nq, 4), 128, 0, st>>>(in, nq, lists, k_in, query_stride, list_stride, k, o); break;
+    }
+    VK_TRY_CUDA(cudaGetLastError());
+    return VK_OK;
+}
+
+int vk_encode_device(int device, const float* centroids, int m, int dsub, const float* d_x, int64_t n,
+                     uint8_t* d_codes, void* stream) {
+    if (!centroids || !d_x || !d_codes) return fail(VK_ERR_INVALID, "pointers must not be NULL");
+    if (m <= 0 || dsub <= 0 || n < 0) return fail(VK_ERR_INVALID, "bad sizes");
+    if (n == 0) return VK_OK;
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t cbytes = (size_t)m * vk::KSUB * dsub * sizeof(float);
+    float* d_cen = nullptr;
+    VK_TRY_CUDA(cudaMallocAsync(&d_cen, cbytes, st));
+    VK_TRY_CUDA(cudaMemcpyAsync(d_cen, centroids, cbytes, cudaMemcpyHostToDevice, st));
+    const size_t smem = (size_t)vk::KSUB * dsub * sizeof(float);
+    if (smem > 48 * 1024)
+        VK_TRY_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(&vk::encode_kernel),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    vk::encode_kernel<<<dim3((unsigned)ceil_div(n, 256), m), 256, smem, st>>>(d_cen, m, dsub, d_x, n, d_codes);
+    VK_TRY_CUDA(cudaGetLastError());
+    VK_TRY_CUDA(cudaFreeAsync(d_cen, st));
+    return VK_OK;
+}
+
+int vk_gen_codes_device(int device, uint64_t seed, const uint32_t* cdf, int clusters, int m, int64_t row_first,
+                        int64_t n, uint8_t* d_codes, void* stream) {
+    if (!cdf || !d_codes || clusters <= 0 || m <= 0 || n < 0 || row_first < 0)
+        return fail(VK_ERR_INVALID, "bad arguments");
+    if (n == 0) return VK_OK;
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t bytes = (size_t)clusters * m * vk::KSUB * sizeof(uint32_t);
+    uint32_t* d_cdf = nullptr;
+    VK_TRY_CUDA(cudaMallocAsync(&d_cdf, bytes, st));
+    VK_TRY_CUDA(cudaMemcpyAsync(d_cdf, cdf, bytes, cudaMemcpyHostToDevice, st));
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    vk::gen_rows_kernel<<<grid_for(n * m, sms), 256, 0, st>>>(vk::mix64(seed), d_cdf, clusters, m, row_first, n,
+                                                              d_codes);
+    VK_TRY_CUDA(cudaGetLastError());
+    VK_TRY_CUDA(cudaFreeAsync(d_cdf, st));
+    return VK_OK;
+}
+
+}  // extern "C"

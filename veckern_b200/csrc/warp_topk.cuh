@@ -1,0 +1,98 @@
+// Warp-cooperative bounded top-k: one sorted list of k (dist, id) pairs per warp, entry e held by lane e % 32 in
+// register e / 32 (S = ceil(k / 32) registers per lane). Same contract as the reference's WarpTopK
+// (src/cuda/kernels.cuh:392-466): k smallest under the (dist, id) order; here k is a run-time value <= 32 * S.
+//
+// Insertion of an admitted candidate: one ballot per register counts the entries below it (its position p),
+// then every entry at or after p moves up by one (shfl_up within a register, lane 31 of register r carrying into
+// lane 0 of register r + 1) and slot p takes the candidate. Entries past k - 1 are never read as results; they
+// only ever hold values that are not below the current threshold, so they never disturb the position count.
+#pragma once
+#include "vk_device.cuh"
+
+namespace vk {
+
+template <int S>
+struct WarpTopK {
+    float d[S];
+    int32_t id[S];
+    float thr_d;  // entry k - 1 (warp-uniform): the admission threshold
+    int32_t thr_i;
+
+    __device__ __forceinline__ void init() {
+#pragma unroll
+        for (int r = 0; r < S; ++r) {
+            d[r] = __int_as_float(0x7f800000);  // +inf
+            id[r] = SENTINEL_ID;
+        }
+        thr_d = __int_as_float(0x7f800000);
+        thr_i = SENTINEL_ID;
+    }
+
+    __device__ __forceinline__ bool admits(float x, int32_t xi) const { return nb_less(x, xi, thr_d, thr_i); }
+
+    // All 32 lanes call with the same (x, xi), which admits() accepted.
+    __device__ __forceinline__ void insert(float x, int32_t xi, int k) {
+        const int lane = threadIdx.x & (WARP - 1);
+        int pos = 0;
+#pragma unroll
+        for (int r = 0; r < S; ++r) pos += __popc(__ballot_sync(FULL, nb_less(d[r], id[r], x, xi)));
+        float carry_d = x;
+        int32_t carry_i = xi;
+#pragma unroll
+        for (int r = 0; r < S; ++r) {
+            float up_d = __shfl_up_sync(FULL, d[r], 1);
+            int32_t up_i = __shfl_up_sync(FULL, id[r], 1);
+            const float last_d = __shfl_sync(FULL, d[r], WARP - 1);
+            const int32_t last_i = __shfl_sync(FULL, id[r], WARP - 1);
+            if (lane == 0) {
+                up_d = carry_d;
+                up_i = carry_i;
+            }
+            const int e = r * WARP + lane;
+            if (e == pos) {
+                d[r] = x;
+                id[r] = xi;
+            } else if (e > pos) {
+                d[r] = up_d;
+                id[r] = up_i;
+            }
+            carry_d = last_d;
+            carry_i = last_i;
+        }
+        const int t = k - 1;
+        float td = d[0];
+        int32_t ti = id[0];
+#pragma unroll
+        for (int r = 1; r < S; ++r)
+            if ((t >> 5) == r) {
+                td = d[r];
+                ti = id[r];
+            }
+        thr_d = __shfl_sync(FULL, td, t & (WARP - 1));
+        thr_i = __shfl_sync(FULL, ti, t & (WARP - 1));
+    }
+
+    // One candidate per lane; admitted ones are inserted one at a time (rare once the list has filled).
+    __device__ __forceinline__ void offer(float x, int32_t xi, bool valid, int k) {
+        unsigned mask = __ballot_sync(FULL, valid && admits(x, xi));
+        while (mask) {
+            const int src = __ffs(mask) - 1;
+            mask &= mask - 1;
+            const float cx = __shfl_sync(FULL, x, src);
+            const int32_t ci = __shfl_sync(FULL, xi, src);
+            if (admits(cx, ci)) insert(cx, ci, k);  // the threshold may have dropped since the ballot
+        }
+    }
+
+    // Writes entries 0 .. k-1 (ascending) as (dist, id) pairs.
+    __device__ __forceinline__ void store(int2* out, int k) const {
+        const int lane = threadIdx.x & (WARP - 1);
+#pragma unroll
+        for (int r = 0; r < S; ++r) {
+            const int e = r * WARP + lane;
+            if (e < k) out[e] = make_int2(__float_as_int(d[r]), id[r]);
+        }
+    }
+};
+
+}  // namespace vk

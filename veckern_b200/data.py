@@ -1,0 +1,77 @@
+"""Input side of the search path on the host: product quantizer and synthetic data (include/vk_host.h).
+
+These produce the database, codebooks and queries the GPU path searches; they are deterministic (counter-based
+or the reference's own std:: engines) so every machine regenerates identical inputs.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from ._native import host, ptr
+
+
+def _ok(rc: int, what: str) -> None:
+    if rc != 0:
+        raise ValueError(f"{what}: bad arguments")
+
+
+def pq_train(x: np.ndarray, m: int, iters: int, seed: int = 1) -> np.ndarray:
+    """The reference's ProductQuantizer::train (src/cpu/pq.cpp:31-69) on all rows of x -> [m, 256, d/m]."""
+    x = np.ascontiguousarray(x, np.float32)
+    n, d = x.shape
+    cent = np.empty((m, 256, d // m), np.float32)
+    _ok(host().vk_host_pq_train(ptr(x), n, d, m, iters, seed, ptr(cent)), "pq_train")
+    return cent
+
+
+def pq_encode(centroids: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """Nearest centroid per sub-space (src/cpu/pq.cpp:71-76) -> [n, m] uint8."""
+    centroids = np.ascontiguousarray(centroids, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    m, _, dsub = centroids.shape
+    codes = np.empty((x.shape[0], m), np.uint8)
+    _ok(host().vk_host_pq_encode(ptr(centroids), m * dsub, m, ptr(x), x.shape[0], ptr(codes)), "pq_encode")
+    return codes
+
+
+def pq_decode(centroids: np.ndarray, codes: np.ndarray) -> np.ndarray:
+    centroids = np.ascontiguousarray(centroids, np.float32)
+    codes = np.ascontiguousarray(codes, np.uint8)
+    m, _, dsub = centroids.shape
+    x = np.empty((codes.shape[0], m * dsub), np.float32)
+    _ok(host().vk_host_pq_decode(ptr(centroids), m * dsub, m, ptr(codes), codes.shape[0], ptr(x)), "pq_decode")
+    return x
+
+
+def synthetic_clustered(n: int, d: int, clusters: int, seed: int) -> np.ndarray:
+    """The reference's Gaussian blobs (src/cpu/io.cpp:54-69), as its test fixtures use them."""
+    out = np.empty((n, d), np.float32)
+    _ok(host().vk_host_synthetic_clustered(n, d, clusters, seed, ptr(out)), "synthetic_clustered")
+    return out
+
+
+def gen_normal(seed: int, rows: int, d: int, row0: int = 0) -> np.ndarray:
+    out = np.empty((rows, d), np.float32)
+    _ok(host().vk_host_gen_normal(seed, row0, rows, d, ptr(out)), "gen_normal")
+    return out
+
+
+def gen_mixture(mix_seed: int, sample_seed: int, rows: int, d: int = 128, ncomp: int = 1000, sigma: float = 12.0,
+                row0: int = 0) -> np.ndarray:
+    out = np.empty((rows, d), np.float32)
+    _ok(host().vk_host_gen_mixture(mix_seed, ncomp, sigma, sample_seed, row0, rows, d, ptr(out)), "gen_mixture")
+    return out
+
+
+def gen_cdf(seed: int, clusters: int, m: int, alpha: float) -> np.ndarray:
+    out = np.empty((clusters, m, 256), np.uint32)
+    _ok(host().vk_host_gen_cdf(seed, clusters, m, alpha, ptr(out)), "gen_cdf")
+    return out
+
+
+def gen_codes(seed: int, cdf: np.ndarray, row0: int, n: int) -> np.ndarray:
+    cdf = np.ascontiguousarray(cdf, np.uint32)
+    clusters, m, _ = cdf.shape
+    out = np.empty((n, m), np.uint8)
+    _ok(host().vk_host_gen_codes(seed, ptr(cdf), clusters, m, row0, n, ptr(out)), "gen_codes")
+    return out

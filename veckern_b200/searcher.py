@@ -1,0 +1,249 @@
+"""Python mirror of the reference's GPU search API (include/veckern/gpu.hpp of shivdeshpande/VecKern) over the
+C ABI: same names, argument meaning and errors (VkError, a RuntimeError, where the reference throws
+std::runtime_error).
+
+    searcher = PQSearcher(centroids, codes)                   # centroids [m, 256, dsub] f32, codes [n, m] u8
+    timings = searcher.search(queries, k, ScanVariant.FusedWarp, out)   # out: [nq, k] NEIGHBOR_DTYPE
+    dist, ids = neighbors_split(out)
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _native as N
+from ._native import NEIGHBOR_DTYPE, VkError, check, lib, ptr
+
+
+class ScanVariant(enum.IntEnum):
+    """include/veckern/gpu.hpp:13-23 of the reference; here only validation rules differ between them."""
+    GlobalLut = 0
+    SharedLut = 1
+    SharedLutVec = 2
+    Interleaved = 3
+    Fused = 4
+    FusedReg = 5
+    FusedVec = 6
+    FusedVecMQ = 7
+    FusedWarp = 8
+
+
+_VARIANT_NAMES = ["v0_global_lut", "v1_shared_lut", "v2_shared_lut_vec", "v3_interleaved", "v4_fused",
+                  "v5_fused_reg", "v6_fused_vec", "v7_fused_vec_mq", "v8_fused_warp"]
+
+
+def variant_name(v: ScanVariant) -> str:
+    return _VARIANT_NAMES[int(v)]
+
+
+def is_fused(v: ScanVariant) -> bool:
+    return ScanVariant.Fused <= v <= ScanVariant.FusedWarp
+
+
+@dataclass
+class Tuning:
+    """include/veckern/gpu.hpp:29-34 of the reference (same defaults and accepted values)."""
+    scan_threads: int = 256
+    blocks_per_query: int = 0
+    queries_per_block: int = 2
+    vectors_per_step: int = 4
+
+    def c(self) -> N.Tuning:
+        return N.Tuning(self.scan_threads, self.blocks_per_query, self.queries_per_block, self.vectors_per_step)
+
+
+@dataclass
+class Timings:
+    transfer_ms: float = 0.0
+    lut_ms: float = 0.0
+    scan_ms: float = 0.0
+    select_ms: float = 0.0
+
+    def kernel_ms(self) -> float:
+        return self.lut_ms + self.scan_ms + self.select_ms
+
+    def total_ms(self) -> float:
+        return self.transfer_ms + self.kernel_ms()
+
+
+@dataclass
+class LaunchShape:
+    threads: int = 0
+    blocks_x: int = 0
+    grid_y: int = 0
+    queries_per_block: int = 1
+    vectors_per_step: int = 1
+    blocks_per_sm: int = 0
+    waves: float = 0.0
+
+
+@dataclass
+class DeviceInfo:
+    name: str
+    sm_count: int
+    peak_bandwidth_gbs: float
+    max_smem_per_block: int
+    clock_mhz: int
+
+
+def device_info(device: int = 0) -> DeviceInfo:
+    d = N.DeviceInfo()
+    check(lib().vk_device_info(device, C.byref(d)), "vk_device_info")
+    return DeviceInfo(d.name.decode(), d.sm_count, d.peak_bandwidth_gbs, d.max_smem_per_block, d.clock_mhz)
+
+
+def neighbors_split(out: np.ndarray):
+    """(dist float32 [..., k], ids int32 [..., k]) views of a NEIGHBOR_DTYPE array."""
+    return out["dist"], out["id"]
+
+
+def empty_neighbors(nq: int, k: int) -> np.ndarray:
+    return np.empty((nq, k), NEIGHBOR_DTYPE)
+
+
+class PQSearcher:
+    """One PQ code database resident on one GPU (include/veckern/gpu.hpp:53-78 of the reference)."""
+
+    def __init__(self, centroids, codes=None, *, device: int = 0, id_base: int = 0, _handle=None):
+        self._h = C.c_void_p()
+        self.tuning = Tuning()
+        self.last = LaunchShape()
+        if _handle is not None:
+            self._h = _handle
+        else:
+            centroids = np.ascontiguousarray(centroids, np.float32)
+            if centroids.ndim != 3 or centroids.shape[1] != 256:
+                raise ValueError("centroids must be [m, 256, dsub] float32")
+            m, _, dsub = centroids.shape
+            if hasattr(codes, "data_ptr"):  # torch tensor already on the device
+                n = codes.shape[0]
+                check(lib().vk_index_create_from_device(device, ptr(centroids), m, dsub, ptr(codes), n, id_base,
+                                                        C.byref(self._h)), "vk_index_create_from_device")
+            else:
+                codes = np.ascontiguousarray(codes, np.uint8)
+                if codes.ndim != 2 or codes.shape[1] != m:
+                    raise ValueError("codes must be [n, m] uint8")
+                check(lib().vk_index_create(device, ptr(centroids), m, dsub, ptr(codes), codes.shape[0], id_base,
+                                            C.byref(self._h)), "vk_index_create")
+        n, m, dsub, base, dev = C.c_int64(), C.c_int(), C.c_int(), C.c_int64(), C.c_int()
+        check(lib().vk_index_info(self._h, C.byref(n), C.byref(m), C.byref(dsub), C.byref(base), C.byref(dev)))
+        self.n, self.m, self.dsub, self.id_base, self.device = n.value, m.value, dsub.value, base.value, dev.value
+        self.d = self.m * self.dsub
+
+    @classmethod
+    def generated(cls, centroids, seed: int, cdf: np.ndarray, row_first: int, n: int, *, device: int = 0,
+                  id_base: int = 0) -> "PQSearcher":
+        """Codes generated on the device (rows [row_first, row_first + n) of the config-3/4 generator)."""
+        centroids = np.ascontiguousarray(centroids, np.float32)
+        cdf = np.ascontiguousarray(cdf, np.uint32)
+        m, _, dsub = centroids.shape
+        h = C.c_void_p()
+        check(lib().vk_index_create_generated(device, ptr(centroids), m, dsub, seed, ptr(cdf), cdf.shape[0],
+                                              row_first, n, id_base, C.byref(h)), "vk_index_create_generated")
+        return cls(None, _handle=h)
+
+    def close(self) -> None:
+        if self._h:
+            lib().vk_index_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def set_tuning(self, tuning: Tuning) -> None:
+        t = tuning.c()
+        check(lib().vk_tuning_validate(C.byref(t)), "set_tuning")
+        self.tuning = tuning
+
+    def last_launch(self) -> LaunchShape:
+        return self.last
+
+    def search(self, queries, k: int, variant: ScanVariant = ScanVariant.FusedWarp, out: np.ndarray | None = None):
+        """HOST queries [nq, d] -> HOST results [nq, k] (NEIGHBOR_DTYPE). Returns (out, Timings)."""
+        queries = np.ascontiguousarray(queries, np.float32).reshape(-1, self.d)
+        nq = queries.shape[0]
+        if out is None:
+            out = empty_neighbors(nq, k)
+        if out.dtype != NEIGHBOR_DTYPE or out.size != nq * k or not out.flags.c_contiguous:
+            raise ValueError("out must be a C-contiguous [nq, k] NEIGHBOR_DTYPE array")
+        t, s, tun = N.Timings(), N.LaunchShape(), self.tuning.c()
+        check(lib().vk_search(self._h, ptr(queries), nq, k, int(variant), C.byref(tun), ptr(out), C.byref(t),
+                              C.byref(s)), "search")
+        if nq:
+            self.last = LaunchShape(s.threads, s.blocks_x, s.grid_y, s.queries_per_block, s.vectors_per_step,
+                                    s.blocks_per_sm, s.waves)
+        return out, Timings(t.transfer_ms, t.lut_ms, t.scan_ms, t.select_ms)
+
+    def distances(self, queries, variant: ScanVariant = ScanVariant.SharedLut, out: np.ndarray | None = None):
+        """HOST queries -> HOST [nq, n] float32 ADC distances (unfused variants only)."""
+        queries = np.ascontiguousarray(queries, np.float32).reshape(-1, self.d)
+        nq = queries.shape[0]
+        if out is None:
+            out = np.empty((nq, self.n), np.float32)
+        t, tun = N.Timings(), self.tuning.c()
+        check(lib().vk_distances(self._h, ptr(queries), nq, int(variant), C.byref(tun), ptr(out), C.byref(t)),
+              "distances")
+        return out, Timings(t.transfer_ms, t.lut_ms, t.scan_ms, t.select_ms)
+
+    # ---- device-resident path (torch tensors on this index's device)
+    def search_device(self, d_queries, k: int, d_out, stream=None, tuning: Tuning | None = None) -> None:
+        """DEVICE queries (torch float32 [nq, d]) -> DEVICE results (torch int64 [nq, k] holding (dist, id)
+        pairs; see device_result_split). Asynchronous on `stream` (a torch.cuda.Stream; default: current)."""
+        nq = d_queries.shape[0]
+        tun = (tuning or self.tuning).c()
+        s = _stream_handle(stream)
+        check(lib().vk_search_device(self._h, ptr(d_queries), nq, k, C.byref(tun), ptr(d_out), s), "search_device")
+
+    def sync(self, stream=None) -> None:
+        check(lib().vk_index_sync(self._h, _stream_handle(stream)), "sync")
+
+    def compute_lut_device(self, d_queries, d_lut, stream=None) -> None:
+        check(lib().vk_compute_lut_device(self._h, ptr(d_queries), d_queries.shape[0], ptr(d_lut),
+                                          _stream_handle(stream)), "compute_lut")
+
+    def get_codes(self, first: int = 0, count: int | None = None) -> np.ndarray:
+        count = self.n - first if count is None else count
+        out = np.empty((count, self.m), np.uint8)
+        check(lib().vk_index_get_codes(self._h, first, count, ptr(out)), "get_codes")
+        return out
+
+
+def _stream_handle(stream):
+    if stream is None:
+        try:
+            import torch
+            return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        except Exception:
+            return None
+    return C.c_void_p(getattr(stream, "cuda_stream", stream))
+
+
+def device_result_split(d_out):
+    """(dist float32, ids int32) views of a torch int64 [nq, k] device result."""
+    import torch
+    v = d_out.view(torch.int32).view(*d_out.shape, 2)
+    return v[..., 0].view(torch.float32), v[..., 1]
+
+
+def merge_topk_device(device: int, d_in, nq: int, lists: int, k_in: int, query_stride: int, list_stride: int,
+                      k: int, d_out, stream=None) -> None:
+    """k best of `lists` sorted candidate lists per query, all in device memory ((dist, id) int64 pairs)."""
+    check(lib().vk_merge_topk_device(device, ptr(d_in), nq, lists, k_in, query_stride, list_stride, k, ptr(d_out),
+                                     _stream_handle(stream)), "merge_topk")
+
+
+__all__ = ["ScanVariant", "Tuning", "Timings", "LaunchShape", "DeviceInfo", "PQSearcher", "VkError",
+           "NEIGHBOR_DTYPE", "device_info", "variant_name", "is_fused", "neighbors_split", "empty_neighbors",
+           "device_result_split", "merge_topk_device"]
