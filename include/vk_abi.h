@@ -65,12 +65,15 @@ typedef struct {
 /* Replaces gpu::Tuning (include/veckern/gpu.hpp:29-34) with the same meaning and the same accepted values
  * (src/cuda/searcher.cu:450-460): scan_threads multiple of 32 in [32, 1024] (used by distances()),
  * blocks_per_query >= 0 (vector chunks per query group; 0 = auto), queries_per_block in {1, 2, 4, 8},
- * vectors_per_step in {1, 2, 4} (32-vector groups each warp holds in flight). */
+ * vectors_per_step in {1, 2, 4} (32-vector groups each warp holds in flight). Added field:
+ * early_abandon (1 = default, 0 = off): stop summing a (query, row) pair once its partial distance exceeds a
+ * proven bound on the query's k-th distance (m in {16, 32, 64}); results are identical either way. */
 typedef struct {
     int scan_threads;
     int blocks_per_query;
     int queries_per_block;
     int vectors_per_step;
+    int early_abandon;
 } vk_tuning_t;
 
 /* Replaces gpu::Timings (include/veckern/gpu.hpp:46-50): milliseconds per stage from CUDA events. */
@@ -132,11 +135,12 @@ int vk_search(vk_index_t* index, const float* queries, int64_t nq, int k, int va
               vk_neighbor_t* out, vk_timings_t* timings, vk_launch_shape_t* shape);
 
 /* Device-resident search: DEVICE queries and results on the caller's CUDA stream (cudaStream_t passed as void*;
- * NULL = the index's own stream). Asynchronous: call vk_index_sync to wait and collect kernel status. */
+ * NULL = the default stream, as in the CUDA runtime). Asynchronous: vk_index_sync waits and collects the kernels'
+ * status. One index's workspace serves one search at a time: searches on different streams must not overlap. */
 int vk_search_device(vk_index_t* index, const float* d_queries, int64_t nq, int k, const vk_tuning_t* tuning,
                      vk_neighbor_t* d_out, void* stream);
 
-/* Waits for the index's work on `stream` (NULL = its own) and reports any kernel-side error. */
+/* Waits for the index's work on `stream` (NULL = the default stream) and reports any kernel-side error. */
 int vk_index_sync(vk_index_t* index, void* stream);
 
 /* Replaces PQSearcher::distances (src/cuda/searcher.cu:522-547): the full nq x n ADC matrix to HOST memory.

@@ -43,7 +43,7 @@ class Port:
         L.vko_adc_search.argtypes = [_f32p, C.c_int, C.c_int, _u8p, _i64, _f32p, _i64, C.c_int, _f32p, _i32p,
                                      C.c_int]
         L.vko_topk_push_all.argtypes = [_f32p, _i32p, _i64, C.c_int, _f32p, _i32p]
-        L.vko_merge_topk.argtypes = [_f32p, _i32p, C.c_int, _i64, C.c_int, _f32p, _i32p]
+        L.vko_merge_topk.argtypes = [_f32p, _i32p, C.c_int, C.c_int, _i64, C.c_int, _f32p, _i32p]
         L.vko_recall_at_k.argtypes = [_i32p, _i64, _i32p, _i64, _i64, C.c_int]
         L.vko_recall_at_k.restype = C.c_double
         L.vko_stream_create.argtypes = [_f32p, _i64, C.c_int, C.c_int]
@@ -97,13 +97,13 @@ class Port:
         return d, i
 
     def merge_topk(self, d, ids, k):
-        """d, ids: [nq, lists, k] -> the k best of the union per query."""
+        """d, ids: [nq, lists, k_in] -> the k best of the union per query."""
         d = _f32(d)
         ids = np.ascontiguousarray(ids, np.int32)
-        nq, lists = d.shape[0], d.shape[1]
+        nq, lists, k_in = d.shape
         od = np.empty((nq, k), np.float32)
         oi = np.empty((nq, k), np.int32)
-        self.lib.vko_merge_topk(d, ids, lists, nq, k, od, oi)
+        self.lib.vko_merge_topk(d, ids, lists, k_in, nq, k, od, oi)
         return od, oi
 
     def recall_at_k(self, found, truth, k):

@@ -190,7 +190,7 @@ void vko_topk_push_all(const float* dists, const int32_t* ids, int64_t count, in
 
 /* Merge of per-shard lists: the union's k best under the same order; padding (id < 0) is skipped, as the
  * reference's select_kernel skips id < 0 candidates (src/cuda/kernels.cuh:193-195). */
-void vko_merge_topk(const float* d, const int32_t* ids, int lists, int64_t nq, int k, float* out_d,
+void vko_merge_topk(const float* d, const int32_t* ids, int lists, int k_in, int64_t nq, int k, float* out_d,
                     int32_t* out_i) {
 #pragma omp parallel
     {
@@ -200,8 +200,8 @@ void vko_merge_topk(const float* d, const int32_t* ids, int lists, int64_t nq, i
         for (int64_t q = 0; q < nq; ++q) {
             topk_t t;
             topk_init(&t, k, hd, hi);
-            const int64_t base = q * (int64_t)lists * k;
-            for (int64_t j = 0; j < (int64_t)lists * k; ++j)
+            const int64_t base = q * (int64_t)lists * k_in;
+            for (int64_t j = 0; j < (int64_t)lists * k_in; ++j)
                 if (ids[base + j] >= 0) topk_push(&t, d[base + j], ids[base + j]);
             topk_write(&t, out_d + q * k, out_i + q * k);
         }

@@ -41,9 +41,9 @@ void vko_adc_search(const float* centroids, int m, int dsub, const uint8_t* code
 void vko_topk_push_all(const float* dists, const int32_t* ids, int64_t count, int k, float* out_d,
                        int32_t* out_i);
 
-/* Merges `lists` sorted lists of k (dist, id) per query (layout [nq][lists][k]) into the k best. Entries with
+/* Merges `lists` lists of k_in (dist, id) per query (layout [nq][lists][k_in]) into the k best. Entries with
  * id < 0 are padding and are skipped. */
-void vko_merge_topk(const float* d, const int32_t* ids, int lists, int64_t nq, int k, float* out_d,
+void vko_merge_topk(const float* d, const int32_t* ids, int lists, int k_in, int64_t nq, int k, float* out_d,
                     int32_t* out_i);
 
 /* Mean |found[:k] ∩ truth[:k]| / k (src/cpu/cpu_ref.cpp:79-91). */

@@ -65,9 +65,11 @@ def test_tuning_defaults_and_rejections():
     lib = N.lib()
     t = N.Tuning()
     lib.vk_tuning_default(C.byref(t))
-    assert (t.scan_threads, t.blocks_per_query, t.queries_per_block, t.vectors_per_step) == (256, 0, 2, 4)
+    assert (t.scan_threads, t.blocks_per_query, t.queries_per_block, t.vectors_per_step, t.early_abandon) == \
+        (256, 0, 2, 4, 1)
     assert lib.vk_tuning_validate(C.byref(t)) == 0
-    for bad in [(100, 0, 2, 1), (256, -1, 2, 1), (256, 0, 3, 1), (256, 0, 2, 3), (0, 0, 2, 1), (1056, 0, 2, 1)]:
+    for bad in [(100, 0, 2, 1, 1), (256, -1, 2, 1, 1), (256, 0, 3, 1, 1), (256, 0, 2, 3, 1), (0, 0, 2, 1, 1),
+                (1056, 0, 2, 1, 1), (256, 0, 2, 1, 2)]:
         assert lib.vk_tuning_validate(C.byref(N.Tuning(*bad))) == N.VK_ERR_INVALID
         assert N.last_error()
 

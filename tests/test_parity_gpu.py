@@ -102,16 +102,36 @@ def test_all_variants_k10(golden, variant):
     assert_same_topk(d, i, g["d_k10"], g["i_k10"], str(variant))
 
 
+@pytest.mark.parametrize("prune", [True, False], ids=["early_abandon", "full_scan"])
 @pytest.mark.parametrize("q", [1, 2, 4, 8])
 @pytest.mark.parametrize("ilp", [1, 2, 4])
 @pytest.mark.parametrize("k", [1, 10, 33, 64, 128])
-def test_every_q_ilp_k(golden, q, ilp, k):
-    """nq = 37 is prime, so every Q > 1 leaves a partial last group (reference tests/test_gpu.cpp:93-101)."""
+def test_every_q_ilp_k(golden, q, ilp, k, prune):
+    """nq = 37 is prime, so every Q > 1 leaves a partial last group (reference tests/test_gpu.cpp:93-101).
+    Both the exact early-abandoning scan and the full scan must give the reference's results."""
     g = golden("gpu_fixture")
     d, i, shape = gpu_search(g["centroids"], g["codes"], g["queries"], k,
-                             tuning=Tuning(queries_per_block=q, vectors_per_step=ilp))
-    assert_same_topk(d, i, g[f"d_k{k}"], g[f"i_k{k}"], f"Q={q} ILP={ilp} k={k}")
+                             tuning=Tuning(queries_per_block=q, vectors_per_step=ilp, early_abandon=prune))
+    assert_same_topk(d, i, g[f"d_k{k}"], g[f"i_k{k}"], f"Q={q} ILP={ilp} k={k} prune={prune}")
     assert shape.queries_per_block == q and shape.grid_y == -(-37 // q)
+
+
+@pytest.mark.parametrize("m,dsub", [(16, 8), (32, 4), (64, 2)])
+@pytest.mark.parametrize("k", [1, 10, 100])
+def test_early_abandon_on_clustered_data(port, m, dsub, k):
+    """Clustered data (where most pairs are abandoned early) with many queries per group: pruned == full ==
+    oracle, bit for bit."""
+    from veckern_b200 import data
+
+    x = data.gen_mixture(0, 0, 30_011, m * dsub, ncomp=100)
+    q = data.gen_mixture(0, 3, 29, m * dsub, ncomp=100)
+    cent = data.pq_train(x[:5000], m, 3, 1)
+    codes = data.pq_encode(cent, x)
+    ed, ei = port.adc_search(cent, codes, q, k)
+    for qpb in (2, 4, 8):
+        for prune in (True, False):
+            d, i, _ = gpu_search(cent, codes, q, k, tuning=Tuning(queries_per_block=qpb, early_abandon=prune))
+            assert_same_topk(d, i, ed, ei, f"m={m} k={k} Q={qpb} prune={prune}")
 
 
 @pytest.mark.parametrize("bpq", [1, 3, 7, 16])
@@ -196,3 +216,93 @@ def test_repeated_searches_are_identical(golden):
         for _ in range(3):
             b, _ = s.search(g["queries"], 100)
             assert np.array_equal(a.view(np.int64), b.view(np.int64))
+
+
+def test_device_path_matches_host_path(golden):
+    """vk_search_device (queries and results in HBM, caller's stream) == vk_search (host buffers)."""
+    import torch
+
+    from veckern_b200 import device_result_split
+
+    g = golden("gpu_fixture")
+    with PQSearcher(g["centroids"], g["codes"]) as s:
+        s.set_tuning(Tuning(queries_per_block=8, vectors_per_step=4))
+        host, _ = s.search(g["queries"], 64)
+        d_q = torch.from_numpy(g["queries"]).cuda()
+        for stream in (None, torch.cuda.Stream()):
+            d_out = torch.empty((d_q.shape[0], 64), dtype=torch.int64, device="cuda")
+            s.search_device(d_q, 64, d_out, stream)
+            s.sync(stream)
+            dd, di = device_result_split(d_out)
+            assert_same_topk(dd.cpu().numpy(), di.cpu().numpy(), host["dist"], host["id"], f"stream {stream}")
+
+
+def test_merge_kernel_matches_oracle(port):
+    import torch
+
+    from veckern_b200 import merge_topk_device
+
+    rng = np.random.default_rng(3)
+    nq, lists, k_in, k = 23, 7, 40, 37
+    d = np.sort(rng.integers(0, 50, size=(nq, lists, k_in)).astype(np.float32), axis=2)  # many ties
+    ids = rng.permutation(nq * lists * k_in).astype(np.int32).reshape(nq, lists, k_in) % 997
+    ids[:, 3, 30:] = -1  # padding entries are skipped
+    # lists must be sorted by (dist, id) for the merge's contract
+    order = np.lexsort((ids, d), axis=2)
+    d = np.take_along_axis(d, order, 2)
+    ids = np.take_along_axis(ids, order, 2)
+    pairs = np.stack([d.view(np.int32), ids], axis=-1).astype(np.int32)
+    d_in = torch.from_numpy(pairs.copy()).cuda().view(torch.int64).reshape(nq, lists, k_in)
+    d_out = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+    merge_topk_device(0, d_in, nq, lists, k_in, lists * k_in, k_in, k, d_out)
+    torch.cuda.synchronize()
+    out = d_out.cpu().numpy().view(np.int32).reshape(nq, k, 2)
+    ed, ei = port.merge_topk(d, ids, k)
+    assert_same_topk(out[..., 0].view(np.float32), out[..., 1], ed, ei, "merge")
+
+
+def test_encode_kernel_matches_host():
+    import torch
+
+    from veckern_b200 import _native as N
+    from veckern_b200 import data
+
+    x = data.gen_mixture(0, 5, 20_000, 128, ncomp=100)
+    cent = data.pq_train(x[:5000], 32, 2, 1)
+    expected = data.pq_encode(cent, x)
+    d_x = torch.from_numpy(x).cuda()
+    d_c = torch.empty((x.shape[0], 32), dtype=torch.uint8, device="cuda")
+    N.check(N.lib().vk_encode_device(0, N.ptr(cent), 32, 4, N.ptr(d_x), x.shape[0], N.ptr(d_c), None), "encode")
+    torch.cuda.synchronize()
+    assert np.array_equal(d_c.cpu().numpy(), expected)
+
+
+def test_generated_database_matches_host_generator(port):
+    """Codes generated on the device == the host generator, and search over them == the oracle."""
+    import torch
+
+    from veckern_b200 import _native as N
+    from veckern_b200 import data
+
+    cdf = data.gen_cdf(4, 64, 16, 0.3)
+    rows0, n = 123_457, 40_009
+    d_c = torch.empty((n, 16), dtype=torch.uint8, device="cuda")
+    N.check(N.lib().vk_gen_codes_device(0, 4, N.ptr(cdf), 64, 16, rows0, n, N.ptr(d_c), None), "gen")
+    torch.cuda.synchronize()
+    host = data.gen_codes(4, cdf, rows0, n)
+    assert np.array_equal(d_c.cpu().numpy(), host)
+    cent = data.gen_normal(6, 16 * 256, 8).reshape(16, 256, 8)
+    q = data.gen_normal(7, 11, 128)
+    with PQSearcher.generated(cent, 4, cdf, rows0, n, id_base=5) as s:
+        assert np.array_equal(s.get_codes(), host)
+        s.set_tuning(Tuning(queries_per_block=4))
+        out, _ = s.search(q, 10)
+    ed, ei = port.adc_search(cent, host, q, 10)
+    assert_same_topk(out["dist"], out["id"] - 5, ed, ei, "generated")
+
+
+def test_index_codes_roundtrip(golden):
+    g = golden("gpu_fixture")
+    with PQSearcher(g["centroids"], g["codes"]) as s:
+        assert np.array_equal(s.get_codes(), g["codes"])
+        assert np.array_equal(s.get_codes(20_000, 11), g["codes"][20_000:])

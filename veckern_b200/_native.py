@@ -35,7 +35,7 @@ class DeviceInfo(C.Structure):
 
 class Tuning(C.Structure):
     _fields_ = [("scan_threads", C.c_int), ("blocks_per_query", C.c_int), ("queries_per_block", C.c_int),
-                ("vectors_per_step", C.c_int)]
+                ("vectors_per_step", C.c_int), ("early_abandon", C.c_int)]
 
 
 class Timings(C.Structure):

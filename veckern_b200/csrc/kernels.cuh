@@ -22,11 +22,11 @@ namespace vk {
 // grid (m, groups), block 256: thread c computes centroid c of sub-space s for the Q queries of group g.
 // Arithmetic of the reference's l2sq (include/veckern/common.hpp:27-34): diff = q - c, acc += diff * diff in
 // j order, each operation rounded on its own (__fsub_rn / __fmul_rn / __fadd_rn: no FMA contraction).
-// Padded query slots (index >= nq) get 0.
+// Padded query slots (index >= nq) get 0. `bound` (optional): the pruned scan's per-query bounds, reset to +inf.
 template <int Q>
 __global__ void __launch_bounds__(256) lut_kernel(const float* __restrict__ centroids,
                                                   const float* __restrict__ queries, int64_t nq, int m, int dsub,
-                                                  float* __restrict__ lut) {
+                                                  float* __restrict__ lut, uint32_t* __restrict__ bound) {
     extern __shared__ float qsub[];  // [Q][dsub]
     const int s = blockIdx.x, g = blockIdx.y, c = threadIdx.x;
     const int64_t d = (int64_t)m * dsub;
@@ -35,6 +35,7 @@ __global__ void __launch_bounds__(256) lut_kernel(const float* __restrict__ cent
         const int64_t qi = (int64_t)g * Q + qq;
         qsub[t] = qi < nq ? queries[qi * d + (int64_t)s * dsub + j] : 0.f;
     }
+    if (bound && s == 0 && c < Q && (int64_t)g * Q + c < nq) bound[(int64_t)g * Q + c] = 0x7f800000u;  // +inf
     __syncthreads();
     const float* cen = centroids + ((int64_t)s * KSUB + c) * dsub;
     float acc[Q];
@@ -72,6 +73,7 @@ struct ScanArgs {
     int2* part;          // [nq][chunks][k] partial lists (dist bits, id)
     int* work_counter;   // dynamic work-item counter, zero before launch
     int* status;         // kernel status word (ERR_* bits)
+    uint32_t* bound;     // [nq] float bits: running upper bound of each query's k-th distance (pruned scan)
     int64_t n, n_pad;    // valid rows, padded rows (multiple of 128)
     int64_t chunk_len;   // rows per chunk, a multiple of 32 * ILP
     int64_t id_base;     // global id = id_base + row
@@ -81,9 +83,10 @@ struct ScanArgs {
 
 // Shared-memory plan of scan_kernel; host and device compute it with the same function.
 struct ScanSmem {
-    uint32_t lut, stage, scratch, bars, flags, total, tile_bytes, lut_bytes;
+    uint32_t lut, stage, scratch, queue, bars, flags, total, tile_bytes, lut_bytes;
 };
-__host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp, int nw, int stages, int k) {
+__host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp, int nw, int stages, int k,
+                                                   bool prune) {
     auto up = [](uint32_t x, uint32_t a) { return (x + a - 1) / a * a; };
     ScanSmem p;
     p.lut_bytes = (uint32_t)Q * m * KSUB * 4u;
@@ -91,11 +94,16 @@ __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp,
     p.lut = 0;
     p.stage = up(p.lut_bytes, 128);
     p.scratch = up(p.stage + (uint32_t)nw * stages * p.tile_bytes, 128);
-    p.bars = up(p.scratch + (uint32_t)nw * k * 8u, 16);
+    p.queue = up(p.scratch + (uint32_t)nw * k * 8u, 16);
+    p.bars = up(p.queue + (prune ? (uint32_t)nw * 32u * ilp * Q * 8u : 0u), 16);
     p.flags = p.bars + (uint32_t)(nw * stages + 1) * 8u;
     p.total = up(p.flags + 16, 128);
     return p;
 }
+
+// Sub-spaces the pruned scan computes for every row before it tests rows against the bounds (phase A). Chosen
+// from the survival curves of partial sums: few (query, row) pairs get past ~5/16 of the sub-spaces.
+__host__ __device__ constexpr int prune_depth(int m) { return m <= 16 ? 5 : m <= 32 ? 9 : 16; }
 
 // One sub-space lookup for Q queries: acc[q] += LUT_q[s][c], rounded per add, in s order.
 template <int Q>
@@ -128,9 +136,20 @@ __device__ __forceinline__ void lookup_add(const unsigned char* lut_smem, int mt
     }
 }
 
+// Byte offset of query q's entry (s = 0, c = 0) in the group's LUT, and the stride between c entries.
+template <int Q>
+__device__ __forceinline__ uint32_t lut_query_base(int q, int mtab) {
+    if constexpr (Q >= 4) return (uint32_t)(q >> 2) * (uint32_t)mtab * KSUB * 16u + (uint32_t)(q & 3) * 4u;
+    else return (uint32_t)q * 4u;
+}
+template <int Q>
+__host__ __device__ constexpr uint32_t lut_entry_bytes() { return Q >= 4 ? 16u : (uint32_t)Q * 4u; }
+
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int b) {
     return b < 4 ? v.x : b < 8 ? v.y : b < 12 ? v.z : v.w;
 }
+
+__device__ __forceinline__ uint32_t code_byte(const uint4& v, int b) { return (word_of(v, b) >> (8 * (b & 3))) & 0xffu; }
 
 // Persistent fused scan + top-k. Work item = (vector chunk, query group), handed out by an atomic counter in
 // chunk-major order, so the blocks running at one time share the same chunk of codes through L2.
@@ -139,14 +158,22 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int b) {
 //              buffers filled by TMA bulk copies (lane 0 issues, mbarrier per slot), computes Q distances per
 //              row with strictly ordered fp32 adds, and offers them to one WarpTopK per query;
 //              the NW warp lists of each query are merged in shared memory into the item's partial list.
+// PRUNE (exact early abandoning): partial sums only grow (every LUT entry is >= +0 and fp32 round-to-nearest
+//   addition is monotone), so a (query, row) pair whose partial sum already exceeds an upper bound T_q of the
+//   query's k-th distance cannot be in the result. T_q = min(the warp list's k-th distance, a per-query global
+//   bound that warps lower with atomicMin). Phase A computes sub-spaces [0, SA) of every row for all Q queries
+//   (LDS.128 lookups); surviving pairs are compacted (ballot + popc) into a per-warp shared-memory queue and
+//   finished 32 at a time, each lane dropping out as soon as its sum exceeds T_q. Results are unchanged.
 // MT: m when it is 16, 32 or 64 (fully unrolled sub-space loop), 0 for any other m.
-template <int Q, int MT, int ILP, int S, int NW>
+template <int Q, int MT, int ILP, int S, int NW, bool PRUNE>
 __global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
+    static_assert(!PRUNE || MT != 0, "the pruned scan is specialised for m = 16, 32, 64");
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int W_T = MT ? (MT + 15) / 16 : 0;
+    constexpr int SA = prune_depth(MT);
     const int m = MT ? MT : a.m;
     const int W = MT ? W_T : a.W;
-    const ScanSmem plan = scan_smem_plan(Q, m, W, ILP, NW, a.stages, a.k);
+    const ScanSmem plan = scan_smem_plan(Q, m, W, ILP, NW, a.stages, a.k, PRUNE);
     unsigned char* lut_smem = smem + plan.lut;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + plan.bars);
     uint64_t* lut_bar = bars + NW * a.stages;
@@ -157,6 +184,7 @@ __global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* my_bars = bars + warp * a.stages;
     unsigned char* my_stages = smem + plan.stage + (uint32_t)warp * a.stages * plan.tile_bytes;
+    int2* my_queue = reinterpret_cast<int2*>(smem + plan.queue) + warp * (32 * ILP * Q);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NW * a.stages + 1; ++i) mbar_init(bars + i, 1);
@@ -198,8 +226,15 @@ __global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
         }
 
         WarpTopK<S> top[Q];
+        float known[Q];  // PRUNE: this warp's view of the global bounds (padded query slots: -1, prune all)
 #pragma unroll
-        for (int q = 0; q < Q; ++q) top[q].init();
+        for (int q = 0; q < Q; ++q) {
+            top[q].init();
+            if constexpr (PRUNE) {
+                const int64_t qi = (int64_t)g * Q + q;
+                known[q] = qi < a.nq ? __uint_as_float(__ldcg(a.bound + qi)) : -1.f;
+            }
+        }
 
         const int64_t t_begin = (int64_t)chunk * a.chunk_len / tile_rows;
         const int64_t t_end = min((int64_t)(chunk + 1) * a.chunk_len, a.n_pad) / tile_rows;
@@ -229,53 +264,139 @@ __global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
             }
             ++consumed;
             const uint4* st = reinterpret_cast<const uint4*>(my_stages + slot * plan.tile_bytes);
-
-            float acc[ILP][Q];
-#pragma unroll
-            for (int u = 0; u < ILP; ++u)
-#pragma unroll
-                for (int q = 0; q < Q; ++q) acc[u][q] = 0.f;
-
-#pragma unroll
-            for (int w = 0; w < (MT ? W_T : 1); ++w) {
-                // generic m: a run-time loop over words; MT: the unrolled loop above with W_T words
-                for (int wr = 0; wr < (MT ? 1 : W); ++wr) {
-                    const int ww = MT ? w : wr;
-                    uint4 cv[ILP];
-#pragma unroll
-                    for (int u = 0; u < ILP; ++u) cv[u] = st[(u * W + ww) * 32 + lane];
-#pragma unroll
-                    for (int b = 0; b < 16; ++b) {
-                        const int s = ww * 16 + b;
-                        if (!MT && s >= m) break;
-#pragma unroll
-                        for (int u = 0; u < ILP; ++u) {
-                            const uint32_t c = (word_of(cv[u], b) >> (8 * (b & 3))) & 0xffu;
-                            lookup_add<Q>(lut_smem, m, s, c, acc[u]);
-                        }
-                    }
-                }
-            }
-            __syncwarp();  // every lane has consumed the slot (the codes fed the lookups above)
-            if (lane == 0 && j + a.stages < my_tiles) issue(j + a.stages);
-
             const int64_t t = t_begin + warp + j * NW;
-            bool any = false;
-            int32_t ids[ILP];
-            bool valid[ILP];
-#pragma unroll
-            for (int u = 0; u < ILP; ++u) {
-                const int64_t row = t * tile_rows + u * 32 + lane;
-                valid[u] = row < a.n;
-                ids[u] = (int32_t)(a.id_base + row);
-#pragma unroll
-                for (int q = 0; q < Q; ++q) any |= valid[u] && top[q].admits(acc[u][q], ids[u]);
-            }
-            if (__any_sync(FULL, any)) {
+            const int64_t tile_row0 = t * tile_rows;
+
+            if constexpr (!PRUNE) {
+                float acc[ILP][Q];
 #pragma unroll
                 for (int u = 0; u < ILP; ++u)
 #pragma unroll
-                    for (int q = 0; q < Q; ++q) top[q].offer(acc[u][q], ids[u], valid[u], a.k);
+                    for (int q = 0; q < Q; ++q) acc[u][q] = 0.f;
+
+#pragma unroll
+                for (int w = 0; w < (MT ? W_T : 1); ++w) {
+                    // generic m: a run-time loop over words; MT: the unrolled loop above with W_T words
+                    for (int wr = 0; wr < (MT ? 1 : W); ++wr) {
+                        const int ww = MT ? w : wr;
+                        uint4 cv[ILP];
+#pragma unroll
+                        for (int u = 0; u < ILP; ++u) cv[u] = st[(u * W + ww) * 32 + lane];
+#pragma unroll
+                        for (int b = 0; b < 16; ++b) {
+                            const int s = ww * 16 + b;
+                            if (!MT && s >= m) break;
+#pragma unroll
+                            for (int u = 0; u < ILP; ++u) lookup_add<Q>(lut_smem, m, s, code_byte(cv[u], b), acc[u]);
+                        }
+                    }
+                }
+                __syncwarp();  // every lane has consumed the slot (the codes fed the lookups above)
+                if (lane == 0 && j + a.stages < my_tiles) issue(j + a.stages);
+
+                bool any = false;
+                int32_t ids[ILP];
+                bool valid[ILP];
+#pragma unroll
+                for (int u = 0; u < ILP; ++u) {
+                    const int64_t row = tile_row0 + u * 32 + lane;
+                    valid[u] = row < a.n;
+                    ids[u] = (int32_t)(a.id_base + row);
+#pragma unroll
+                    for (int q = 0; q < Q; ++q) any |= valid[u] && top[q].admits(acc[u][q], ids[u]);
+                }
+                if (__any_sync(FULL, any)) {
+#pragma unroll
+                    for (int u = 0; u < ILP; ++u)
+#pragma unroll
+                        for (int q = 0; q < Q; ++q) top[q].offer(acc[u][q], ids[u], valid[u], a.k);
+                }
+            } else {
+                // ---- phase A: sub-spaces [0, SA) of every row, all Q queries per fetch
+                float acc[ILP][Q];
+#pragma unroll
+                for (int u = 0; u < ILP; ++u)
+#pragma unroll
+                    for (int q = 0; q < Q; ++q) acc[u][q] = 0.f;
+                uint4 cv[ILP];
+#pragma unroll
+                for (int s = 0; s < SA; ++s) {
+                    if (s % 16 == 0) {
+#pragma unroll
+                        for (int u = 0; u < ILP; ++u) cv[u] = st[(u * W_T + s / 16) * 32 + lane];
+                    }
+#pragma unroll
+                    for (int u = 0; u < ILP; ++u) lookup_add<Q>(lut_smem, MT, s, code_byte(cv[u], s % 16), acc[u]);
+                }
+                float bnd[Q];
+#pragma unroll
+                for (int q = 0; q < Q; ++q) {
+                    const int64_t qi = (int64_t)g * Q + q;
+                    if (qi < a.nq) known[q] = fminf(known[q], __uint_as_float(__ldcg(a.bound + qi)));
+                    bnd[q] = fminf(known[q], top[q].thr_d);
+                }
+                // ---- compaction of the surviving (row, query) pairs
+                const unsigned lt = (1u << lane) - 1u;
+                int cnt = 0;
+#pragma unroll
+                for (int u = 0; u < ILP; ++u) {
+                    const bool valid = tile_row0 + u * 32 + lane < a.n;
+#pragma unroll
+                    for (int q = 0; q < Q; ++q) {
+                        const bool alive = valid && !(acc[u][q] > bnd[q]);
+                        const unsigned msk = __ballot_sync(FULL, alive);
+                        if (alive)
+                            my_queue[cnt + __popc(msk & lt)] = make_int2(__float_as_int(acc[u][q]), (u * 32 + lane) | (q << 16));
+                        cnt += __popc(msk);
+                    }
+                }
+                __syncwarp();
+                // ---- phase B: finish the queued pairs, 32 at a time, dropping each as soon as it exceeds its bound
+                for (int base = 0; base < cnt; base += 32) {
+                    const int e = base + lane;
+                    bool live = e < cnt;
+                    const int2 ent = live ? my_queue[e] : make_int2(0, 0);
+                    float x = __int_as_float(ent.x);
+                    const int r = ent.y & 0xffff, q = ent.y >> 16;
+                    float bq = bnd[0];
+#pragma unroll
+                    for (int qq = 1; qq < Q; ++qq)
+                        if (q == qq) bq = bnd[qq];
+                    const unsigned char* lq = lut_smem + lut_query_base<Q>(q, MT);
+                    const uint4* rowp = st + (r >> 5) * W_T * 32 + (r & 31);
+                    uint4 cw = make_uint4(0, 0, 0, 0);
+#pragma unroll
+                    for (int s = SA; s < MT; ++s) {
+                        if (s == SA || s % 16 == 0) {
+                            if (!__any_sync(FULL, live)) break;
+                            if (live) cw = rowp[(s / 16) * 32];
+                        }
+                        if (live) {
+                            const uint32_t c = code_byte(cw, s % 16);
+                            x = __fadd_rn(x, *reinterpret_cast<const float*>(lq + ((uint32_t)s * KSUB + c) * lut_entry_bytes<Q>()));
+                            live = !(x > bq);
+                        }
+                        if ((s - SA) % 4 == 3 && !__any_sync(FULL, live)) break;
+                    }
+                    const int32_t id = (int32_t)(a.id_base + tile_row0 + r);
+#pragma unroll
+                    for (int qq = 0; qq < Q; ++qq) {
+                        if (__any_sync(FULL, live && q == qq)) {
+                            top[qq].offer(x, id, live && q == qq, a.k);
+                            bnd[qq] = fminf(bnd[qq], top[qq].thr_d);
+                        }
+                    }
+                }
+                __syncwarp();  // the queue and the stage slot are free again
+                if (lane == 0 && j + a.stages < my_tiles) issue(j + a.stages);
+                // Publish improved list thresholds as global bounds for the other warps and blocks.
+#pragma unroll
+                for (int q = 0; q < Q; ++q) {
+                    if (top[q].thr_d < known[q]) {
+                        if (lane == 0) atomicMin(a.bound + (int64_t)g * Q + q, __float_as_uint(top[q].thr_d));
+                        known[q] = top[q].thr_d;
+                    }
+                }
             }
         }
         if (warp_abort && lane == 0) {

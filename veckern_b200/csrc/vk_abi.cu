@@ -105,12 +105,12 @@ const char* variant_name(int v) {
     return v >= 0 && v <= 8 ? names[v] : "unknown";
 }
 
-const void* scan_kernel_ptr(int Q, int mt, int ilp, int s) {
+const void* scan_kernel_ptr(int Q, int mt, int ilp, int s, bool prune) {
     switch (Q) {
-        case 1: return vk::scan_kernel_for<1>(mt, ilp, s);
-        case 2: return vk::scan_kernel_for<2>(mt, ilp, s);
-        case 4: return vk::scan_kernel_for<4>(mt, ilp, s);
-        case 8: return vk::scan_kernel_for<8>(mt, ilp, s);
+        case 1: return vk::scan_kernel_for<1>(mt, ilp, s, prune);
+        case 2: return vk::scan_kernel_for<2>(mt, ilp, s, prune);
+        case 4: return vk::scan_kernel_for<4>(mt, ilp, s, prune);
+        case 8: return vk::scan_kernel_for<8>(mt, ilp, s, prune);
         default: return nullptr;
     }
 }
@@ -146,6 +146,7 @@ struct vk_index {
     cudaStream_t stream = nullptr;
     DevBuf<float> queries, lut, dists;
     DevBuf<int2> part, out;
+    DevBuf<uint32_t> bound;  // per-query running bound of the k-th distance (pruned scan)
     int* flags = nullptr;  // [0] work counter, [1] kernel status word
     cudaEvent_t ev[6] = {};
     int sm_count = 0, smem_optin = 0, clock_khz = 0;
@@ -166,6 +167,7 @@ namespace {
 
 struct Plan {
     int Q = 1, ilp = 1, stages = kStagesMax, S = 1, mt = 0;
+    bool prune = false;
     int threads = 0, blocks_per_sm = 0, grid = 0;
     int groups = 0, chunks = 0;
     int64_t chunk_len = 0;
@@ -181,27 +183,30 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     p.threads = nw * 32;
     p.S = s_for_k(k);
     p.mt = (ix->m == 16 || ix->m == 32 || ix->m == 64) ? ix->m : 0;
+    // Exact early abandoning: specialised for m in {16, 32, 64}; its compaction queue holds 1 or 2 row groups.
+    p.prune = t.early_abandon != 0 && p.mt != 0;
     int Q = t.queries_per_block;
     int64_t need = 1;
     while (need < nq && need < 8) need *= 2;
     Q = (int)std::min<int64_t>(Q, need);
-    p.ilp = t.vectors_per_step;
+    const int ilp_req = p.prune ? std::min(t.vectors_per_step, 2) : t.vectors_per_step;
+    p.ilp = ilp_req;
     p.stages = kStagesMax;
     auto fits = [&](int q, int ilp, int st) {
-        return vk::scan_smem_plan(q, ix->m, ix->W, ilp, nw, st, k).total <= (uint32_t)ix->smem_optin;
+        return vk::scan_smem_plan(q, ix->m, ix->W, ilp, nw, st, k, p.prune).total <= (uint32_t)ix->smem_optin;
     };
     for (;;) {
         if (fits(Q, p.ilp, p.stages)) break;
         if (p.stages > 2) { --p.stages; continue; }
         if (p.ilp > 1) { p.ilp /= 2; p.stages = kStagesMax; continue; }
-        if (Q > 1) { Q /= 2; p.ilp = t.vectors_per_step; p.stages = kStagesMax; continue; }
+        if (Q > 1) { Q /= 2; p.ilp = ilp_req; p.stages = kStagesMax; continue; }
         return fail(VK_ERR_INVALID, "LUT does not fit in shared memory (m = %d needs %u bytes, device allows %d)",
-                    ix->m, vk::scan_smem_plan(1, ix->m, ix->W, 1, nw, 2, k).total, ix->smem_optin);
+                    ix->m, vk::scan_smem_plan(1, ix->m, ix->W, 1, nw, 2, k, p.prune).total, ix->smem_optin);
     }
     p.Q = Q;
-    p.fn = scan_kernel_ptr(Q, p.mt, p.ilp, p.S);
+    p.fn = scan_kernel_ptr(Q, p.mt, p.ilp, p.S, p.prune);
     if (!p.fn) return fail(VK_ERR_UNSUPPORTED, "no scan kernel for Q=%d m=%d ilp=%d", Q, ix->m, p.ilp);
-    p.smem = vk::scan_smem_plan(Q, ix->m, ix->W, p.ilp, nw, p.stages, k).total;
+    p.smem = vk::scan_smem_plan(Q, ix->m, ix->W, p.ilp, nw, p.stages, k, p.prune).total;
     VK_TRY_CUDA(cudaFuncSetAttribute(p.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
     int per_sm = 0;
     VK_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, p.fn, p.threads, p.smem));
@@ -248,6 +253,7 @@ int validate_tuning(const vk_tuning_t* t) {
         return fail(VK_ERR_INVALID, "queries_per_block must be 1, 2, 4 or 8");
     if (!(t->vectors_per_step == 1 || t->vectors_per_step == 2 || t->vectors_per_step == 4))
         return fail(VK_ERR_INVALID, "vectors_per_step must be 1, 2 or 4");
+    if (t->early_abandon != 0 && t->early_abandon != 1) return fail(VK_ERR_INVALID, "early_abandon must be 0 or 1");
     return VK_OK;
 }
 
@@ -268,6 +274,7 @@ int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk
     const int64_t lut_floats = (int64_t)p.groups * p.Q * ix->m * vk::KSUB;
     VK_TRY(ix->lut.ensure(lut_floats));
     VK_TRY(ix->part.ensure((size_t)nq * p.chunks * k));
+    VK_TRY(ix->bound.ensure((size_t)nq));
 
     // LUT
     {
@@ -276,8 +283,10 @@ int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk
         if (smem > 48 * 1024) VK_TRY_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         const float* cen = ix->centroids;
         float* lut = ix->lut.ptr;
+        uint32_t* bound = p.prune ? ix->bound.ptr : nullptr;
         int m = ix->m, dsub = ix->dsub;
-        void* args[] = {(void*)&cen, (void*)&d_queries, (void*)&nq, (void*)&m, (void*)&dsub, (void*)&lut};
+        void* args[] = {(void*)&cen, (void*)&d_queries, (void*)&nq, (void*)&m, (void*)&dsub, (void*)&lut,
+                        (void*)&bound};
         VK_TRY_CUDA(cudaLaunchKernel(fn, dim3(ix->m, p.groups), dim3(vk::KSUB), args, smem, st));
     }
     if (marks) VK_TRY_CUDA(cudaEventRecord(marks[0], st));
@@ -290,6 +299,7 @@ int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk
         a.part = ix->part.ptr;
         a.work_counter = ix->flags;
         a.status = ix->flags + 1;
+        a.bound = ix->bound.ptr;
         a.n = ix->n;
         a.n_pad = ix->n_pad;
         a.chunk_len = p.chunk_len;
@@ -407,6 +417,7 @@ void vk_tuning_default(vk_tuning_t* t) {
     t->blocks_per_query = 0;
     t->queries_per_block = 2;
     t->vectors_per_step = 4;
+    t->early_abandon = 1;
 }
 
 int vk_tuning_validate(const vk_tuning_t* t) {
@@ -617,14 +628,14 @@ int vk_search_device(vk_index_t* ix, const float* d_queries, int64_t nq, int k, 
     if (nq == 0) return VK_OK;
     DeviceGuard guard(ix->device);
     if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ix->stream;
-    return run_search(ix, d_queries, nq, k, t, reinterpret_cast<int2*>(d_out), st, nullptr, nullptr);
+    return run_search(ix, d_queries, nq, k, t, reinterpret_cast<int2*>(d_out), static_cast<cudaStream_t>(stream),
+                      nullptr, nullptr);
 }
 
 int vk_index_sync(vk_index_t* ix, void* stream) {
     if (!ix) return fail(VK_ERR_INVALID, "index must not be NULL");
     DeviceGuard guard(ix->device);
-    return read_status(ix, stream ? static_cast<cudaStream_t>(stream) : ix->stream);
+    return read_status(ix, static_cast<cudaStream_t>(stream));
 }
 
 int vk_distances(vk_index_t* ix, const float* queries, int64_t nq, int variant, const vk_tuning_t* tuning,
@@ -663,7 +674,7 @@ int vk_distances(vk_index_t* ix, const float* queries, int64_t nq, int variant, 
                                     cudaMemcpyHostToDevice, st));
         VK_TRY_CUDA(cudaEventRecord(ev[1], st));
         vk::lut_kernel<1><<<dim3(ix->m, (unsigned)b), vk::KSUB, ix->dsub * sizeof(float), st>>>(
-            ix->centroids, ix->queries.ptr, b, ix->m, ix->dsub, ix->lut.ptr);
+            ix->centroids, ix->queries.ptr, b, ix->m, ix->dsub, ix->lut.ptr, nullptr);
         VK_TRY_CUDA(cudaGetLastError());
         VK_TRY_CUDA(cudaEventRecord(ev[2], st));
         const int threads = t.scan_threads;
@@ -694,9 +705,9 @@ int vk_compute_lut_device(vk_index_t* ix, const float* d_queries, int64_t nq, fl
     if (!d_queries || !d_lut) return fail(VK_ERR_INVALID, "queries and lut must not be NULL");
     if (nq > 65535) return fail(VK_ERR_INVALID, "at most 65535 queries per call");
     DeviceGuard guard(ix->device);
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ix->stream;
-    vk::lut_kernel<1><<<dim3(ix->m, (unsigned)nq), vk::KSUB, ix->dsub * sizeof(float), st>>>(ix->centroids, d_queries,
-                                                                                             nq, ix->m, ix->dsub, d_lut);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    vk::lut_kernel<1><<<dim3(ix->m, (unsigned)nq), vk::KSUB, ix->dsub * sizeof(float), st>>>(
+        ix->centroids, d_queries, nq, ix->m, ix->dsub, d_lut, nullptr);
     VK_TRY_CUDA(cudaGetLastError());
     return VK_OK;
 }

@@ -50,9 +50,11 @@ class Tuning:
     blocks_per_query: int = 0
     queries_per_block: int = 2
     vectors_per_step: int = 4
+    early_abandon: bool = True  # exact pruning by partial sums (results identical); False = full scan
 
     def c(self) -> N.Tuning:
-        return N.Tuning(self.scan_threads, self.blocks_per_query, self.queries_per_block, self.vectors_per_step)
+        return N.Tuning(self.scan_threads, self.blocks_per_query, self.queries_per_block, self.vectors_per_step,
+                        int(self.early_abandon))
 
 
 @dataclass
@@ -221,12 +223,10 @@ class PQSearcher:
 
 
 def _stream_handle(stream):
+    """cudaStream_t of a torch.cuda.Stream / raw handle; None -> torch's current stream (0 = default stream)."""
     if stream is None:
-        try:
-            import torch
-            return C.c_void_p(torch.cuda.current_stream().cuda_stream)
-        except Exception:
-            return None
+        import torch
+        return C.c_void_p(torch.cuda.current_stream().cuda_stream)
     return C.c_void_p(getattr(stream, "cuda_stream", stream))
 
 
