@@ -26,7 +26,8 @@ namespace vk {
 template <int Q>
 __global__ void __launch_bounds__(256) lut_kernel(const float* __restrict__ centroids,
                                                   const float* __restrict__ queries, int64_t nq, int m, int dsub,
-                                                  float* __restrict__ lut, uint32_t* __restrict__ bound) {
+                                                  float* __restrict__ lut, uint32_t* __restrict__ bound,
+                                                  int2* __restrict__ glist, int* __restrict__ glock, int k) {
     extern __shared__ float qsub[];  // [Q][dsub]
     const int s = blockIdx.x, g = blockIdx.y, c = threadIdx.x;
     const int64_t d = (int64_t)m * dsub;
@@ -35,7 +36,16 @@ __global__ void __launch_bounds__(256) lut_kernel(const float* __restrict__ cent
         const int64_t qi = (int64_t)g * Q + qq;
         qsub[t] = qi < nq ? queries[qi * d + (int64_t)s * dsub + j] : 0.f;
     }
-    if (bound && s == 0 && c < Q && (int64_t)g * Q + c < nq) bound[(int64_t)g * Q + c] = 0x7f800000u;  // +inf
+    if (bound && s == 0) {  // reset the pruned scan's per-query state: bound +inf, empty global list, lock free
+        for (int t = c; t < Q * k; t += blockDim.x) {
+            const int64_t qi = (int64_t)g * Q + t / k;
+            if (qi < nq) glist[qi * k + t % k] = make_int2(0x7f800000, SENTINEL_ID);
+        }
+        if (c < Q && (int64_t)g * Q + c < nq) {
+            bound[(int64_t)g * Q + c] = 0x7f800000u;
+            glock[(int64_t)g * Q + c] = 0;
+        }
+    }
     __syncthreads();
     const float* cen = centroids + ((int64_t)s * KSUB + c) * dsub;
     float acc[Q];
@@ -74,19 +84,23 @@ struct ScanArgs {
     int* work_counter;   // dynamic work-item counter, zero before launch
     int* status;         // kernel status word (ERR_* bits)
     uint32_t* bound;     // [nq] float bits: running upper bound of each query's k-th distance (pruned scan)
+    int2* glist;         // [nq][k] best (dist, id) pairs of the chunks merged so far (pruned scan)
+    int* glock;          // [nq] try-locks of glist (0 = free)
     int64_t n, n_pad;    // valid rows, padded rows (multiple of 128)
     int64_t chunk_len;   // rows per chunk, a multiple of 32 * ILP
     int64_t id_base;     // global id = id_base + row
     int m, W, nq, groups, chunks, k, stages;
+    int merge_slots;        // 1 or Q (see scan_smem_plan)
     long long wait_budget;  // SM cycles a bounded wait may take
 };
 
-// Shared-memory plan of scan_kernel; host and device compute it with the same function.
+// Shared-memory plan of scan_kernel; host and device compute it with the same function. merge_slots: how many
+// queries' warp lists the item-end merge stages at once (1 or Q).
 struct ScanSmem {
-    uint32_t lut, stage, scratch, queue, bars, flags, total, tile_bytes, lut_bytes;
+    uint32_t lut, stage, scratch, queue, ring, bars, flags, total, tile_bytes, lut_bytes;
 };
 __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp, int nw, int stages, int k,
-                                                   bool prune) {
+                                                   bool prune, int merge_slots) {
     auto up = [](uint32_t x, uint32_t a) { return (x + a - 1) / a * a; };
     ScanSmem p;
     p.lut_bytes = (uint32_t)Q * m * KSUB * 4u;
@@ -94,8 +108,10 @@ __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp,
     p.lut = 0;
     p.stage = up(p.lut_bytes, 128);
     p.scratch = up(p.stage + (uint32_t)nw * stages * p.tile_bytes, 128);
-    p.queue = up(p.scratch + (uint32_t)nw * k * 8u, 16);
-    p.bars = up(p.queue + (prune ? (uint32_t)nw * 32u * ilp * Q * 8u : 0u), 16);
+    p.queue = up(p.scratch + (uint32_t)merge_slots * nw * k * 8u, 16);
+    // the queue holds at most half a tile's (row, query) pairs: with more survivors the tile is finished in full
+    p.ring = up(p.queue + (prune ? (uint32_t)nw * 16u * ilp * Q * 8u : 0u), 16);
+    p.bars = up(p.ring + (uint32_t)nw * stages * 4u, 16);
     p.flags = p.bars + (uint32_t)(nw * stages + 1) * 8u;
     p.total = up(p.flags + 16, 128);
     return p;
@@ -103,7 +119,7 @@ __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp,
 
 // Sub-spaces the pruned scan computes for every row before it tests rows against the bounds (phase A). Chosen
 // from the survival curves of partial sums: few (query, row) pairs get past ~5/16 of the sub-spaces.
-__host__ __device__ constexpr int prune_depth(int m) { return m <= 16 ? 5 : m <= 32 ? 9 : 16; }
+__host__ __device__ constexpr int prune_depth(int m) { return m <= 16 ? 6 : m <= 32 ? 10 : 20; }
 
 // One sub-space lookup for Q queries: acc[q] += LUT_q[s][c], rounded per add, in s order.
 template <int Q>
@@ -154,37 +170,46 @@ __device__ __forceinline__ uint32_t code_byte(const uint4& v, int b) { return (w
 // Persistent fused scan + top-k. Work item = (vector chunk, query group), handed out by an atomic counter in
 // chunk-major order, so the blocks running at one time share the same chunk of codes through L2.
 //   per item:  (group changed) TMA bulk copy of the group's Q LUTs into shared memory;
-//              each warp streams its 32*ILP-row tiles of the chunk through a private ring of `stages` shared
-//              buffers filled by TMA bulk copies (lane 0 issues, mbarrier per slot), computes Q distances per
-//              row with strictly ordered fp32 adds, and offers them to one WarpTopK per query;
-//              the NW warp lists of each query are merged in shared memory into the item's partial list.
+//              warps take the chunk's 32*ILP-row tiles from a block counter and stream each through a private
+//              ring of `stages` shared buffers filled by TMA bulk copies (lane 0 issues, one mbarrier per slot),
+//              compute Q distances per row with strictly ordered fp32 adds, and offer them to one WarpTopK per
+//              query; at the end the NW warp lists of each query are merged into the item's partial list.
 // PRUNE (exact early abandoning): partial sums only grow (every LUT entry is >= +0 and fp32 round-to-nearest
 //   addition is monotone), so a (query, row) pair whose partial sum already exceeds an upper bound T_q of the
 //   query's k-th distance cannot be in the result. T_q = min(the warp list's k-th distance, a per-query global
-//   bound that warps lower with atomicMin). Phase A computes sub-spaces [0, SA) of every row for all Q queries
-//   (LDS.128 lookups); surviving pairs are compacted (ballot + popc) into a per-warp shared-memory queue and
-//   finished 32 at a time, each lane dropping out as soon as its sum exceeds T_q. Results are unchanged.
+//   bound: the k-th distance of a global list into which every finished item folds its own list). Phase A
+//   computes sub-spaces [0, SA) of every row for all Q queries (LDS.128 lookups); when at most half of the
+//   (row, query) pairs survive, the survivors are compacted (ballot + popc) into a per-warp shared-memory queue
+//   and finished 32 at a time, each lane dropping out as soon as its sum exceeds T_q; otherwise the whole tile
+//   is finished with the Q-wide lookups. Results are unchanged.
 // MT: m when it is 16, 32 or 64 (fully unrolled sub-space loop), 0 for any other m.
+// Two blocks share an SM whenever the group's LUT leaves room for that, so registers are capped at 128.
+template <int Q, int MT>
+constexpr int scan_min_blocks() { return Q * (MT ? MT : 16) * KSUB * 4 <= 80 * 1024 ? 2 : 1; }
+
 template <int Q, int MT, int ILP, int S, int NW, bool PRUNE>
-__global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
+__global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel(const ScanArgs a) {
     static_assert(!PRUNE || MT != 0, "the pruned scan is specialised for m = 16, 32, 64");
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int W_T = MT ? (MT + 15) / 16 : 0;
     constexpr int SA = prune_depth(MT);
+    static_assert(!PRUNE || SA % 2 == 0, "phase B fetches sub-spaces in pairs inside one 16-byte word");
     const int m = MT ? MT : a.m;
     const int W = MT ? W_T : a.W;
-    const ScanSmem plan = scan_smem_plan(Q, m, W, ILP, NW, a.stages, a.k, PRUNE);
+    const ScanSmem plan = scan_smem_plan(Q, m, W, ILP, NW, a.stages, a.k, PRUNE, a.merge_slots);
     unsigned char* lut_smem = smem + plan.lut;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + plan.bars);
     uint64_t* lut_bar = bars + NW * a.stages;
     int* s_item = reinterpret_cast<int*>(smem + plan.flags);
     int* s_abort = s_item + 1;
+    int* s_tile = s_item + 2;
     int2* scratch = reinterpret_cast<int2*>(smem + plan.scratch);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* my_bars = bars + warp * a.stages;
     unsigned char* my_stages = smem + plan.stage + (uint32_t)warp * a.stages * plan.tile_bytes;
-    int2* my_queue = reinterpret_cast<int2*>(smem + plan.queue) + warp * (32 * ILP * Q);
+    int2* my_queue = reinterpret_cast<int2*>(smem + plan.queue) + warp * (16 * ILP * Q);
+    int* my_ring = reinterpret_cast<int*>(smem + plan.ring) + warp * a.stages;  // tile held by each slot, -1: none
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NW * a.stages + 1; ++i) mbar_init(bars + i, 1);
@@ -199,7 +224,10 @@ __global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
     int cur_g = -1;
 
     for (;;) {
-        if (threadIdx.x == 0) *s_item = atomicAdd(a.work_counter, 1);
+        if (threadIdx.x == 0) {
+            *s_item = atomicAdd(a.work_counter, 1);
+            *s_tile = 0;
+        }
         __syncthreads();  // (A) previous item finished by every warp; the LUT may be replaced
         const int item = *s_item;
         if (item >= items || *s_abort) break;
@@ -237,24 +265,35 @@ __global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
         }
 
         const int64_t t_begin = (int64_t)chunk * a.chunk_len / tile_rows;
-        const int64_t t_end = min((int64_t)(chunk + 1) * a.chunk_len, a.n_pad) / tile_rows;
-        const int64_t my_tiles = t_end - t_begin > warp ? (t_end - t_begin - warp + NW - 1) / NW : 0;
+        const int ntiles = (int)(min((int64_t)(chunk + 1) * a.chunk_len, a.n_pad) / tile_rows - t_begin);
 
-        auto issue = [&](int64_t j) {  // lane 0: tile j of this warp into the next ring slot
-            const int64_t t = t_begin + warp + j * NW;
+        // lane 0: take the chunk's next tile (if any) into the next ring slot
+        auto refill = [&]() {
             const uint32_t slot = issued % (uint32_t)a.stages;
-            fence_proxy_async_smem();
-            mbar_arrive_expect_tx(my_bars + slot, plan.tile_bytes);
-            bulk_g2s(my_stages + slot * plan.tile_bytes, a.codes + t * tile_rows * W, plan.tile_bytes,
-                     my_bars + slot);
-            ++issued;
+            const int t = atomicAdd(s_tile, 1);
+            if (t < ntiles) {
+                my_ring[slot] = t;
+                fence_proxy_async_smem();
+                mbar_arrive_expect_tx(my_bars + slot, plan.tile_bytes);
+                bulk_g2s(my_stages + slot * plan.tile_bytes, a.codes + (t_begin + t) * tile_rows * W,
+                         plan.tile_bytes, my_bars + slot);
+                ++issued;
+            } else {
+                my_ring[slot] = -1;
+            }
         };
         bool warp_abort = __any_sync(FULL, *s_abort != 0);
         if (lane == 0 && !warp_abort)
-            for (int64_t j = 0; j < (my_tiles < a.stages ? my_tiles : (int64_t)a.stages); ++j) issue(j);
-        __syncwarp();
-        for (int64_t j = 0; j < my_tiles && !warp_abort; ++j) {
+            for (int j = 0; j < a.stages; ++j) {  // fill the ring; stop at the first slot marked empty
+                const uint32_t before = issued;
+                refill();
+                if (issued == before) break;
+            }
+        while (!warp_abort) {
+            __syncwarp();  // ring entries written by lane 0 are visible
             const uint32_t slot = consumed % (uint32_t)a.stages;
+            const int tile = my_ring[slot];
+            if (tile < 0 || consumed == __shfl_sync(FULL, issued, 0)) break;  // the chunk has no tiles left
             const uint32_t parity = (consumed / (uint32_t)a.stages) & 1u;
             if (!__all_sync(FULL, mbar_wait_bounded(my_bars + slot, parity, a.wait_budget))) {
                 if (lane == 0) atomicOr(a.status, ERR_WAIT_TIMEOUT);
@@ -264,8 +303,7 @@ __global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
             }
             ++consumed;
             const uint4* st = reinterpret_cast<const uint4*>(my_stages + slot * plan.tile_bytes);
-            const int64_t t = t_begin + warp + j * NW;
-            const int64_t tile_row0 = t * tile_rows;
+            const int64_t tile_row0 = (t_begin + tile) * tile_rows;
 
             if constexpr (!PRUNE) {
                 float acc[ILP][Q];
@@ -292,7 +330,7 @@ __global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
                     }
                 }
                 __syncwarp();  // every lane has consumed the slot (the codes fed the lookups above)
-                if (lane == 0 && j + a.stages < my_tiles) issue(j + a.stages);
+                if (lane == 0) refill();
 
                 bool any = false;
                 int32_t ids[ILP];
@@ -335,23 +373,61 @@ __global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
                     if (qi < a.nq) known[q] = fminf(known[q], __uint_as_float(__ldcg(a.bound + qi)));
                     bnd[q] = fminf(known[q], top[q].thr_d);
                 }
-                // ---- compaction of the surviving (row, query) pairs
-                const unsigned lt = (1u << lane) - 1u;
-                int cnt = 0;
+                // ---- surviving (row, query) pairs
+                unsigned masks[ILP][Q];
+                int total = 0;
 #pragma unroll
                 for (int u = 0; u < ILP; ++u) {
                     const bool valid = tile_row0 + u * 32 + lane < a.n;
 #pragma unroll
                     for (int q = 0; q < Q; ++q) {
-                        const bool alive = valid && !(acc[u][q] > bnd[q]);
-                        const unsigned msk = __ballot_sync(FULL, alive);
-                        if (alive)
-                            my_queue[cnt + __popc(msk & lt)] = make_int2(__float_as_int(acc[u][q]), (u * 32 + lane) | (q << 16));
-                        cnt += __popc(msk);
+                        masks[u][q] = __ballot_sync(FULL, valid && !(acc[u][q] > bnd[q]));
+                        total += __popc(masks[u][q]);
                     }
                 }
+                int cnt = 0;
+                if (2 * total > 32 * ILP * Q) {
+                    // Most pairs survive (no tight bound yet): finishing every row with the Q-wide lookups of the
+                    // full scan is cheaper than finishing pairs one query per lane.
+#pragma unroll
+                    for (int s = SA; s < MT; ++s) {
+                        if (s % 16 == 0) {
+#pragma unroll
+                            for (int u = 0; u < ILP; ++u) cv[u] = st[(u * W_T + s / 16) * 32 + lane];
+                        }
+#pragma unroll
+                        for (int u = 0; u < ILP; ++u)
+                            lookup_add<Q>(lut_smem, MT, s, code_byte(cv[u], s % 16), acc[u]);
+                    }
+                    bool any = false;
+                    int32_t ids[ILP];
+#pragma unroll
+                    for (int u = 0; u < ILP; ++u) {
+                        ids[u] = (int32_t)(a.id_base + tile_row0 + u * 32 + lane);
+#pragma unroll
+                        for (int q = 0; q < Q; ++q) any |= ((masks[u][q] >> lane) & 1u) && top[q].admits(acc[u][q], ids[u]);
+                    }
+                    if (__any_sync(FULL, any)) {
+#pragma unroll
+                        for (int u = 0; u < ILP; ++u)
+#pragma unroll
+                            for (int q = 0; q < Q; ++q) top[q].offer(acc[u][q], ids[u], (masks[u][q] >> lane) & 1u, a.k);
+                    }
+                } else {
+                    const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+                    for (int u = 0; u < ILP; ++u)
+#pragma unroll
+                        for (int q = 0; q < Q; ++q) {
+                            if ((masks[u][q] >> lane) & 1u)
+                                my_queue[cnt + __popc(masks[u][q] & lt)] =
+                                    make_int2(__float_as_int(acc[u][q]), (u * 32 + lane) | (q << 16));
+                            cnt += __popc(masks[u][q]);
+                        }
+                }
                 __syncwarp();
-                // ---- phase B: finish the queued pairs, 32 at a time, dropping each as soon as it exceeds its bound
+                // ---- phase B: finish the queued pairs 32 at a time, two sub-spaces per step, each lane dropping out
+                // as soon as its sum exceeds its query's bound
                 for (int base = 0; base < cnt; base += 32) {
                     const int e = base + lane;
                     bool live = e < cnt;
@@ -366,17 +442,22 @@ __global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
                     const uint4* rowp = st + (r >> 5) * W_T * 32 + (r & 31);
                     uint4 cw = make_uint4(0, 0, 0, 0);
 #pragma unroll
-                    for (int s = SA; s < MT; ++s) {
+                    for (int s = SA; s < MT; s += 2) {
                         if (s == SA || s % 16 == 0) {
                             if (!__any_sync(FULL, live)) break;
                             if (live) cw = rowp[(s / 16) * 32];
+                        } else if ((s - SA) % 4 == 0 && !__any_sync(FULL, live)) {
+                            break;
                         }
                         if (live) {
-                            const uint32_t c = code_byte(cw, s % 16);
-                            x = __fadd_rn(x, *reinterpret_cast<const float*>(lq + ((uint32_t)s * KSUB + c) * lut_entry_bytes<Q>()));
+                            const uint32_t c0 = code_byte(cw, s % 16), c1 = code_byte(cw, (s + 1) % 16);
+                            const float v0 = *reinterpret_cast<const float*>(lq + ((uint32_t)s * KSUB + c0) * lut_entry_bytes<Q>());
+                            const float v1 = *reinterpret_cast<const float*>(lq + ((uint32_t)(s + 1) * KSUB + c1) * lut_entry_bytes<Q>());
+                            x = __fadd_rn(x, v0);
                             live = !(x > bq);
+                            x = __fadd_rn(x, v1);
+                            live = live && !(x > bq);
                         }
-                        if ((s - SA) % 4 == 3 && !__any_sync(FULL, live)) break;
                     }
                     const int32_t id = (int32_t)(a.id_base + tile_row0 + r);
 #pragma unroll
@@ -388,7 +469,7 @@ __global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
                     }
                 }
                 __syncwarp();  // the queue and the stage slot are free again
-                if (lane == 0 && j + a.stages < my_tiles) issue(j + a.stages);
+                if (lane == 0) refill();
                 // Publish improved list thresholds as global bounds for the other warps and blocks.
 #pragma unroll
                 for (int q = 0; q < Q; ++q) {
@@ -411,25 +492,58 @@ __global__ void __launch_bounds__(NW * 32, 1) scan_kernel(const ScanArgs a) {
 
         __syncthreads();  // (B) all warps finished the item's tiles; s_abort is stable
         if (*s_abort) continue;  // uniform: the next (A) exits the loop
-        // Merge the NW warp lists of each query into the item's partial list.
-#pragma unroll
-        for (int q = 0; q < Q; ++q) {
-            const int64_t qi = (int64_t)g * Q + q;
-            if (qi < a.nq) {  // uniform
-                top[q].store(scratch + warp * a.k, a.k);
-                __syncthreads();
-                if (warp == 0) {
-                    WarpTopK<S> mt;
-                    mt.init();
-                    const int total = NW * a.k;
-                    for (int j0 = 0; j0 < total; j0 += 32) {
+        // Merge the NW warp lists of each query into the item's partial list: merge_slots queries at a time,
+        // query q0 + j merged by warp j.
+        auto merge_and_publish = [&](int64_t qi, const int2* slot_lists) {
+            WarpTopK<S> mt;
+            mt.init();
+            const int total = NW * a.k;
+            for (int j0 = 0; j0 < total; j0 += 32) {
+                const int j = j0 + lane;
+                const int2 e = j < total ? slot_lists[j] : make_int2(0x7f800000, SENTINEL_ID);
+                mt.offer(__int_as_float(e.x), e.y, j < total, a.k);
+            }
+            mt.store(a.part + (qi * a.chunks + chunk) * a.k, a.k);  // this item's own list
+            if constexpr (PRUNE) {
+                // Fold the item's list into the query's global list of the best pairs seen so far, whose k-th
+                // distance bounds the query for every other warp. Chunks cover disjoint rows, so the union has
+                // no duplicates. If another block holds the lock the fold is skipped: only the bound gets
+                // weaker, never wrong.
+                int got = 0;
+                if (lane == 0) got = atomicCAS(a.glock + qi, 0, 1) == 0;
+                if (__shfl_sync(FULL, got, 0)) {
+                    __threadfence();
+                    int2* gl = a.glist + qi * a.k;
+                    for (int j0 = 0; j0 < a.k; j0 += 32) {
                         const int j = j0 + lane;
-                        const int2 e = j < total ? scratch[j] : make_int2(0x7f800000, SENTINEL_ID);
-                        mt.offer(__int_as_float(e.x), e.y, j < total, a.k);
+                        const int2 e = j < a.k ? __ldcg(gl + j) : make_int2(0x7f800000, SENTINEL_ID);
+                        mt.offer(__int_as_float(e.x), e.y, j < a.k, a.k);
                     }
-                    mt.store(a.part + (qi * a.chunks + chunk) * a.k, a.k);
+                    mt.store(gl, a.k);
+                    __threadfence();
+                    __syncwarp();
+                    if (lane == 0) atomicExch(a.glock + qi, 0);
                 }
-                __syncthreads();
+                if (lane == 0 && mt.thr_i != SENTINEL_ID) atomicMin(a.bound + qi, __float_as_uint(mt.thr_d));
+            }
+        };
+        if (a.merge_slots >= Q) {
+#pragma unroll
+            for (int q = 0; q < Q; ++q) top[q].store(scratch + (q * NW + warp) * a.k, a.k);
+            __syncthreads();
+            const int64_t qi = (int64_t)g * Q + warp;
+            if (warp < Q && qi < a.nq) merge_and_publish(qi, scratch + warp * NW * a.k);
+            __syncthreads();
+        } else {
+#pragma unroll
+            for (int q = 0; q < Q; ++q) {
+                const int64_t qi = (int64_t)g * Q + q;
+                if (qi < a.nq) {  // uniform
+                    top[q].store(scratch + warp * a.k, a.k);
+                    __syncthreads();
+                    if (warp == 0) merge_and_publish(qi, scratch);
+                    __syncthreads();
+                }
             }
         }
     }

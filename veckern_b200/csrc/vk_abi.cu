@@ -147,6 +147,8 @@ struct vk_index {
     DevBuf<float> queries, lut, dists;
     DevBuf<int2> part, out;
     DevBuf<uint32_t> bound;  // per-query running bound of the k-th distance (pruned scan)
+    DevBuf<int2> glist;      // per-query global best-k list (pruned scan)
+    DevBuf<int> glock;       // per-query try-locks of glist
     int* flags = nullptr;  // [0] work counter, [1] kernel status word
     cudaEvent_t ev[6] = {};
     int sm_count = 0, smem_optin = 0, clock_khz = 0;
@@ -166,7 +168,7 @@ struct vk_index {
 namespace {
 
 struct Plan {
-    int Q = 1, ilp = 1, stages = kStagesMax, S = 1, mt = 0;
+    int Q = 1, ilp = 1, stages = kStagesMax, S = 1, mt = 0, merge_slots = 1;
     bool prune = false;
     int threads = 0, blocks_per_sm = 0, grid = 0;
     int groups = 0, chunks = 0;
@@ -192,8 +194,10 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     const int ilp_req = p.prune ? std::min(t.vectors_per_step, 2) : t.vectors_per_step;
     p.ilp = ilp_req;
     p.stages = kStagesMax;
+    auto slots = [&](int q) { return (uint32_t)q * nw * k * 8u <= 16384u ? q : 1; };  // parallel item merges
     auto fits = [&](int q, int ilp, int st) {
-        return vk::scan_smem_plan(q, ix->m, ix->W, ilp, nw, st, k, p.prune).total <= (uint32_t)ix->smem_optin;
+        return vk::scan_smem_plan(q, ix->m, ix->W, ilp, nw, st, k, p.prune, slots(q)).total <=
+               (uint32_t)ix->smem_optin;
     };
     for (;;) {
         if (fits(Q, p.ilp, p.stages)) break;
@@ -201,12 +205,13 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
         if (p.ilp > 1) { p.ilp /= 2; p.stages = kStagesMax; continue; }
         if (Q > 1) { Q /= 2; p.ilp = ilp_req; p.stages = kStagesMax; continue; }
         return fail(VK_ERR_INVALID, "LUT does not fit in shared memory (m = %d needs %u bytes, device allows %d)",
-                    ix->m, vk::scan_smem_plan(1, ix->m, ix->W, 1, nw, 2, k, p.prune).total, ix->smem_optin);
+                    ix->m, vk::scan_smem_plan(1, ix->m, ix->W, 1, nw, 2, k, p.prune, 1).total, ix->smem_optin);
     }
     p.Q = Q;
     p.fn = scan_kernel_ptr(Q, p.mt, p.ilp, p.S, p.prune);
     if (!p.fn) return fail(VK_ERR_UNSUPPORTED, "no scan kernel for Q=%d m=%d ilp=%d", Q, ix->m, p.ilp);
-    p.smem = vk::scan_smem_plan(Q, ix->m, ix->W, p.ilp, nw, p.stages, k, p.prune).total;
+    p.merge_slots = slots(Q);
+    p.smem = vk::scan_smem_plan(Q, ix->m, ix->W, p.ilp, nw, p.stages, k, p.prune, p.merge_slots).total;
     VK_TRY_CUDA(cudaFuncSetAttribute(p.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
     int per_sm = 0;
     VK_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, p.fn, p.threads, p.smem));
@@ -217,7 +222,9 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     const int64_t tile_rows = 32 * p.ilp;
     const int64_t tiles = ix->n_pad / tile_rows;
     const int64_t max_chunks = std::max<int64_t>(1, tiles / (2 * nw));  // >= 2 tiles per warp per chunk
-    const int64_t min_chunks = std::min(max_chunks, ceil_div(ix->n_pad, kMaxRowsPerChunk));
+    // The pruned scan tightens each query's bound as chunks complete: use enough chunks for that to pay off.
+    const int64_t min_chunks =
+        std::min(max_chunks, std::max<int64_t>(ceil_div(ix->n_pad, kMaxRowsPerChunk), p.prune ? 48 : 1));
     int64_t chunks = min_chunks;
     if (t.blocks_per_query > 0) {
         chunks = std::min<int64_t>(t.blocks_per_query, max_chunks);
@@ -275,6 +282,8 @@ int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk
     VK_TRY(ix->lut.ensure(lut_floats));
     VK_TRY(ix->part.ensure((size_t)nq * p.chunks * k));
     VK_TRY(ix->bound.ensure((size_t)nq));
+    VK_TRY(ix->glist.ensure((size_t)nq * k));
+    VK_TRY(ix->glock.ensure((size_t)nq));
 
     // LUT
     {
@@ -284,9 +293,11 @@ int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk
         const float* cen = ix->centroids;
         float* lut = ix->lut.ptr;
         uint32_t* bound = p.prune ? ix->bound.ptr : nullptr;
-        int m = ix->m, dsub = ix->dsub;
+        int2* glist = ix->glist.ptr;
+        int* glock = ix->glock.ptr;
+        int m = ix->m, dsub = ix->dsub, kk = k;
         void* args[] = {(void*)&cen, (void*)&d_queries, (void*)&nq, (void*)&m, (void*)&dsub, (void*)&lut,
-                        (void*)&bound};
+                        (void*)&bound, (void*)&glist, (void*)&glock, (void*)&kk};
         VK_TRY_CUDA(cudaLaunchKernel(fn, dim3(ix->m, p.groups), dim3(vk::KSUB), args, smem, st));
     }
     if (marks) VK_TRY_CUDA(cudaEventRecord(marks[0], st));
@@ -300,6 +311,8 @@ int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk
         a.work_counter = ix->flags;
         a.status = ix->flags + 1;
         a.bound = ix->bound.ptr;
+        a.glist = ix->glist.ptr;
+        a.glock = ix->glock.ptr;
         a.n = ix->n;
         a.n_pad = ix->n_pad;
         a.chunk_len = p.chunk_len;
@@ -311,6 +324,7 @@ int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk
         a.chunks = p.chunks;
         a.k = k;
         a.stages = p.stages;
+        a.merge_slots = p.merge_slots;
         a.wait_budget = ix->wait_budget;
         void* args[] = {(void*)&a};
         VK_TRY_CUDA(cudaLaunchKernel(p.fn, dim3(p.grid), dim3(p.threads), args, p.smem, st));
@@ -674,7 +688,7 @@ int vk_distances(vk_index_t* ix, const float* queries, int64_t nq, int variant, 
                                     cudaMemcpyHostToDevice, st));
         VK_TRY_CUDA(cudaEventRecord(ev[1], st));
         vk::lut_kernel<1><<<dim3(ix->m, (unsigned)b), vk::KSUB, ix->dsub * sizeof(float), st>>>(
-            ix->centroids, ix->queries.ptr, b, ix->m, ix->dsub, ix->lut.ptr, nullptr);
+            ix->centroids, ix->queries.ptr, b, ix->m, ix->dsub, ix->lut.ptr, nullptr, nullptr, nullptr, 0);
         VK_TRY_CUDA(cudaGetLastError());
         VK_TRY_CUDA(cudaEventRecord(ev[2], st));
         const int threads = t.scan_threads;
@@ -707,7 +721,7 @@ int vk_compute_lut_device(vk_index_t* ix, const float* d_queries, int64_t nq, fl
     DeviceGuard guard(ix->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     vk::lut_kernel<1><<<dim3(ix->m, (unsigned)nq), vk::KSUB, ix->dsub * sizeof(float), st>>>(
-        ix->centroids, d_queries, nq, ix->m, ix->dsub, d_lut, nullptr);
+        ix->centroids, d_queries, nq, ix->m, ix->dsub, d_lut, nullptr, nullptr, nullptr, 0);
     VK_TRY_CUDA(cudaGetLastError());
     return VK_OK;
 }
