@@ -169,6 +169,21 @@ int vk_encode_device(int device, const float* centroids, int m, int dsub, const 
 int vk_gen_codes_device(int device, uint64_t seed, const uint32_t* cdf, int clusters, int m, int64_t row_first,
                         int64_t n, uint8_t* d_codes, void* stream);
 
+/* No counterpart in the reference. A device-resident search that allocates nothing, for callers that must not
+ * call cudaMalloc or cudaFree: code running where an allocation would synchronise the device and stall other
+ * streams (latency-bound serving threads), or under an allocator the process has handed all memory to.
+ * Same inputs and output as vk_search_device (the index built beforehand, DEVICE queries, DEVICE results), but
+ * the search's working memory (LUTs, per-chunk lists, pruning state) lives in one fixed array of
+ * VK_NOALLOC_SCRATCH_BYTES compiled into the library, which every GPU that loads the library holds until the
+ * process exits. Calls needing more than that (about nq * m KiB of LUTs plus nq * k * (chunks + 2) * 8 bytes of
+ * lists) are rejected with VK_ERR_INVALID; split the queries. The first call on a device looks the array's
+ * address up (make that first call before any stream capture). Runs on `stream` (NULL = the default stream) and
+ * returns when the results are written. All calls share the one array: calls that overlap on the GPU (other host
+ * threads, other streams) race and must not be made. */
+#define VK_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+int vk_search_noalloc(vk_index_t* index, const float* d_queries, int64_t nq, int k, const vk_tuning_t* tuning,
+                      vk_neighbor_t* d_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

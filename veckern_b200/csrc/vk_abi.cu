@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstring>
 #include <limits>
+#include <mutex>
 #include <string>
 
 #include "../../include/vk_abi.h"
@@ -790,3 +791,132 @@ int vk_gen_codes_device(int device, uint64_t seed, const uint32_t* cdf, int clus
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------ no allocation
+// vk_search_noalloc: the search with its working memory in g_noalloc_scratch instead of the index's buffers.
+// Host code cannot use the array's name as a device address; its address is looked up per device with
+// cudaGetSymbolAddress (the device current) and cached. Nothing here calls cudaMalloc, cudaFree or any
+// allocating routine.
+namespace {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[VK_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mutex;
+constexpr int kNoAllocMaxDevices = 64;
+unsigned char* g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+int noalloc_scratch_address(int device, unsigned char** out) {
+    if (device < 0 || device >= kNoAllocMaxDevices) return fail(VK_ERR_UNSUPPORTED, "device %d out of range", device);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_addr[device]) {
+        void* addr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+        if (e != cudaSuccess)
+            return fail(VK_ERR_CUDA, "cudaGetSymbolAddress(scratch) on device %d failed: %s", device, cudaGetErrorString(e));
+        g_noalloc_addr[device] = static_cast<unsigned char*>(addr);
+    }
+    *out = g_noalloc_addr[device];
+    return VK_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+}  // namespace
+
+extern "C" int vk_search_noalloc(vk_index_t* ix, const float* d_queries, int64_t nq, int k, const vk_tuning_t* tuning,
+                                 vk_neighbor_t* d_out, void* stream) {
+    if (!ix) return fail(VK_ERR_INVALID, "index must not be NULL");
+    if (k < 1 || k > 128 || (int64_t)k > ix->n) return fail(VK_ERR_INVALID, "k must be in [1, min(128, n)]");
+    if (nq < 0) return fail(VK_ERR_INVALID, "nq must be >= 0");
+    if (nq > 0 && (!d_queries || !d_out)) return fail(VK_ERR_INVALID, "queries and out must not be NULL");
+    vk_tuning_t t;
+    vk_tuning_default(&t);
+    if (tuning) t = *tuning;
+    VK_TRY(validate_tuning(&t));
+    if (nq == 0) return VK_OK;
+    if (nq > max_query_batch(ix))
+        return fail(VK_ERR_INVALID, "nq %lld exceeds the batch limit %lld", (long long)nq, (long long)max_query_batch(ix));
+    DeviceGuard guard(ix->device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
+    unsigned char* base = nullptr;
+    VK_TRY(noalloc_scratch_address(ix->device, &base));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+    Plan p;
+    VK_TRY(plan_scan(ix, nq, k, t, p));
+    // Carve the array: LUTs | per-chunk lists | bounds | global lists | locks | counter + status.
+    const size_t o_lut = 0;
+    const size_t o_part = o_lut + align256((size_t)p.groups * p.Q * ix->m * vk::KSUB * sizeof(float));
+    const size_t o_bound = o_part + align256((size_t)nq * p.chunks * k * sizeof(int2));
+    const size_t o_glist = o_bound + align256((size_t)nq * sizeof(uint32_t));
+    const size_t o_glock = o_glist + align256((size_t)nq * k * sizeof(int2));
+    const size_t o_flags = o_glock + align256((size_t)nq * sizeof(int));
+    const size_t need = o_flags + align256(2 * sizeof(int));
+    if (need > VK_NOALLOC_SCRATCH_BYTES)
+        return fail(VK_ERR_INVALID,
+                    "this search needs %zu bytes of working memory; vk_search_noalloc has %zu (search fewer queries "
+                    "per call)",
+                    need, (size_t)VK_NOALLOC_SCRATCH_BYTES);
+    float* lut = reinterpret_cast<float*>(base + o_lut);
+    int2* part = reinterpret_cast<int2*>(base + o_part);
+    uint32_t* bound = reinterpret_cast<uint32_t*>(base + o_bound);
+    int2* glist = reinterpret_cast<int2*>(base + o_glist);
+    int* glock = reinterpret_cast<int*>(base + o_glock);
+    int* flags = reinterpret_cast<int*>(base + o_flags);
+
+    // The array keeps the previous call's contents: the work counter and the status word start at zero; the LUT
+    // kernel rewrites the LUTs and, for the pruned scan, resets the bounds, global lists and locks.
+    VK_TRY_CUDA(cudaMemsetAsync(flags, 0, 2 * sizeof(int), st));
+    {
+        const void* fn = lut_kernel_ptr(p.Q);
+        const size_t smem = (size_t)p.Q * ix->dsub * sizeof(float);
+        if (smem > 48 * 1024) VK_TRY_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        const float* cen = ix->centroids;
+        uint32_t* bnd = p.prune ? bound : nullptr;
+        int m = ix->m, dsub = ix->dsub, kk = k;
+        void* args[] = {(void*)&cen, (void*)&d_queries, (void*)&nq, (void*)&m, (void*)&dsub, (void*)&lut,
+                        (void*)&bnd, (void*)&glist, (void*)&glock, (void*)&kk};
+        VK_TRY_CUDA(cudaLaunchKernel(fn, dim3(ix->m, p.groups), dim3(vk::KSUB), args, smem, st));
+    }
+    {
+        vk::ScanArgs a{};
+        a.codes = ix->codes;
+        a.lut = lut;
+        a.part = part;
+        a.work_counter = flags;
+        a.status = flags + 1;
+        a.bound = bound;
+        a.glist = glist;
+        a.glock = glock;
+        a.n = ix->n;
+        a.n_pad = ix->n_pad;
+        a.chunk_len = p.chunk_len;
+        a.id_base = ix->id_base;
+        a.m = ix->m;
+        a.W = ix->W;
+        a.nq = (int)nq;
+        a.groups = p.groups;
+        a.chunks = p.chunks;
+        a.k = k;
+        a.stages = p.stages;
+        a.merge_slots = p.merge_slots;
+        a.wait_budget = ix->wait_budget;
+        void* args[] = {(void*)&a};
+        VK_TRY_CUDA(cudaLaunchKernel(p.fn, dim3(p.grid), dim3(p.threads), args, p.smem, st));
+    }
+    {
+        const void* fn = merge_kernel_ptr(p.S);
+        const int2* in = part;
+        int2* o = reinterpret_cast<int2*>(d_out);
+        int lists = p.chunks, k_in = k, kk = k;
+        int64_t qstride = (int64_t)p.chunks * k, lstride = k;
+        void* args[] = {(void*)&in, (void*)&nq, (void*)&lists, (void*)&k_in, (void*)&qstride, (void*)&lstride,
+                        (void*)&kk, (void*)&o};
+        VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)ceil_div(nq, 4)), dim3(128), args, 0, st));
+    }
+    int status = 0;
+    VK_TRY_CUDA(cudaMemcpyAsync(&status, flags + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
+    VK_TRY_CUDA(cudaStreamSynchronize(st));
+    if (status != 0) return fail(VK_ERR_DEVICE, "kernel reported status 0x%x (a bounded wait ran out)", status);
+    return VK_OK;
+}
