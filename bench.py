@@ -20,7 +20,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import signal
 import subprocess
@@ -49,6 +48,8 @@ def parse():
     p.add_argument("--ilp", type=int, default=2, help="32-row groups per warp step")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample duration")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--verify", action="store_true",
+                   help="rank 0 also searches the whole database on its GPU and checks the merged result bit-exactly")
     return p.parse_args()
 
 
@@ -131,11 +132,15 @@ def lookup_wavefront_model(codes: np.ndarray, Q: int, sample_rows: int = 1 << 17
 
 # ------------------------------------------------------------------------------------------------ workload
 def build_workload(args, rank: int, world: int):
+    """This rank's shard of the configuration (generated row range only; same codebooks on every rank)."""
     from veckern_b200 import configs
+    from veckern_b200.shard import shard_of
 
     spec = configs.spec(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k)
-    w = configs.make(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k, encode=gpu_encoder())
-    return spec, w
+    sh = shard_of(spec["n"], world, rank)
+    w = configs.make(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k, encode=gpu_encoder(),
+                     rows=(sh.lo, sh.hi))
+    return spec, w, sh
 
 
 def gpu_encoder():
@@ -222,13 +227,12 @@ def run_ours(args):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
-    spec, w = build_workload(args, rank, world)
+    spec, w, sh = build_workload(args, rank, world)
     n, m, nq, k = spec["n"], spec["m"], spec["nq"], spec["k"]
-    shard = math.ceil(n / world)
-    lo, hi = rank * shard, min(n, (rank + 1) * shard)
+    lo, hi = sh.lo, sh.hi
     tuning = Tuning(queries_per_block=args.qpb, vectors_per_step=args.ilp)
     if w.codes is not None:
-        s = PQSearcher(w.centroids, w.codes[lo:hi], device=local, id_base=lo)
+        s = PQSearcher(w.centroids, w.codes, device=local, id_base=lo)
     else:
         s = PQSearcher.generated(w.centroids, spec["code_seed"], w.cdf, lo, hi - lo, device=local, id_base=lo)
     s.set_tuning(tuning)
@@ -240,11 +244,19 @@ def run_ours(args):
     d_final = torch.empty((nq, k), dtype=torch.int64, device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
 
+    from veckern_b200.shard import gather_and_merge
+
+    def exchange():
+        """One all-gather of the per-shard lists over NCCL, then the GPU merge into d_final."""
+        def merge(buf, lay):
+            merge_topk_device(local, buf, nq, lay["lists"], lay["k_in"], lay["query_stride"], lay["list_stride"], k,
+                              d_final, stream)
+        gather_and_merge(d_local, d_gather, nq, k, lambda buf, x: dist.all_gather_into_tensor(buf, x), merge)
+
     def step_device(tun=None):
         s.search_device(d_q, k, d_local, stream, tuning=tun)
         if world > 1:
-            dist.all_gather_into_tensor(d_gather, d_local)
-            merge_topk_device(local, d_gather, nq, world, k, k, nq * k, k, d_final, stream)
+            exchange()
 
     for _ in range(args.warmup):
         step_device()
@@ -300,8 +312,7 @@ def run_ours(args):
         _, t = s.search(h_q, k, out=h_out)  # synchronous: H2D, LUT, scan, merge, D2H
         if world > 1:
             d_local.copy_(torch.from_numpy(h_out.view(np.int64)), non_blocking=True)
-            dist.all_gather_into_tensor(d_gather, d_local)
-            merge_topk_device(local, d_gather, nq, world, k, k, nq * k, k, d_final, stream)
+            exchange()
             h_final.copy_(d_final, non_blocking=True)
         t1.record(stream)
         torch.cuda.synchronize()
@@ -322,6 +333,25 @@ def run_ours(args):
     s.set_tuning(tuning)
     clk = clocks.stop()
 
+    verified = None
+    if args.verify and world > 1:
+        # the gathered + merged result of the last device step against one GPU over the whole database
+        s.search_device(d_q, k, d_local, stream)
+        exchange()
+        torch.cuda.synchronize()
+        if rank == 0:
+            from veckern_b200 import configs
+            full = configs.make(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k, encode=gpu_encoder())
+            with PQSearcher(full.centroids, full.codes, device=local) as one:
+                one.set_tuning(tuning)
+                ref = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+                one.search_device(d_q, k, ref, stream)
+                one.sync(stream)
+            verified = bool(torch.equal(ref, d_final))
+            if not verified:
+                raise SystemExit("multi-GPU merged result differs from the single-GPU search")
+        dist.barrier()
+
     dev_ms_t = torch.tensor([dev_ms, float(np.sum(e2e_ms)), float(np.mean(scan_ms)), full_ms,
                              float(np.mean(full_scan_ms))], device="cuda")
     if world > 1:
@@ -338,7 +368,7 @@ def run_ours(args):
         achieved = lookups / (scan_mean / 1e3)
         smem_peak_bytes = 128.0 * info.sm_count * sm_mhz * 1e6
         Q = s.last_launch().queries_per_block
-        codes_for_model = w.codes[lo:hi] if w.codes is not None else None
+        codes_for_model = w.codes if w.codes is not None else None
         wf = lookup_wavefront_model(codes_for_model, Q) if codes_for_model is not None else None
         per_fetch = 4 if Q >= 4 else Q  # lookups served per warp LUT fetch per lane
         fetches = lookups / 32.0 / per_fetch
@@ -380,6 +410,7 @@ def run_ours(args):
                           "note": "early abandoning off: every (query, row, sub-space) lookup executed"},
             "gpu_launches": args.steps * (3 + (1 if world > 1 else 0)),
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
+            "verified_against_single_gpu": verified,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

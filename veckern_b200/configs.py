@@ -61,24 +61,30 @@ def spec(name: str, **overrides) -> dict:
 
 
 def make(name: str, *, n: int | None = None, m: int | None = None, nq: int | None = None, k: int | None = None,
-         keep_base: bool = False, encode=None) -> Workload:
+         keep_base: bool = False, encode=None, rows: tuple[int, int] | None = None) -> Workload:
     """Generates config `name` (optionally resized). encode(centroids, x) -> codes may be given to encode on the
-    GPU (veckern_b200.gpu_encode); the default encodes on the host."""
+    GPU; the default encodes on the host. rows=(lo, hi): only that shard of the database is generated and encoded
+    (codes[i] is row lo + i); the codebooks are the same as for the whole database."""
     s = spec(name, n=n, m=m, nq=nq, k=k)
     d = s["d"]
+    lo, hi = rows if rows is not None else (0, s["n"])
     if s["kind"] == "generated":
         cent = data.gen_normal(s["centroid_seed"], s["m"] * 256, d // s["m"]).reshape(s["m"], 256, d // s["m"])
         q = data.gen_normal(s["query_seed"], s["nq"], d)
         cdf = data.gen_cdf(s["code_seed"], s["clusters"], s["m"], s["alpha"])
         return Workload(name, s, cent, q, cdf=cdf)
     if s["kind"] == "normal":
-        x = data.gen_normal(s["data_seed"], s["n"], d)
+        x = data.gen_normal(s["data_seed"], s["n"], d)  # training draws from all rows
         q = data.gen_normal(s["query_seed"], s["nq"], d)
         train = x
+        x = x[lo:hi]
     else:
-        x = data.gen_mixture(s["mix_seed"], s["mix_seed"], s["n"], d)
+        x = data.gen_mixture(s["mix_seed"], s["mix_seed"], hi - lo, d, row0=lo)
         q = data.gen_mixture(s["mix_seed"], s["query_seed"], s["nq"], d)
-        train = x[: min(s["train_rows"], s["n"])]
+        t = min(s["train_rows"], s["n"])
+        train = x[:t] if lo == 0 and hi >= t else data.gen_mixture(s["mix_seed"], s["mix_seed"], t, d)
     cent = data.pq_train(train, s["m"], s["pq_iters"], s["pq_seed"])
     codes = (encode or data.pq_encode)(cent, x)
-    return Workload(name, s, cent, q, codes=codes, base=x if keep_base else None)
+    w = Workload(name, s, cent, q, codes=codes, base=x if keep_base else None)
+    w.extra["row0"] = lo
+    return w
