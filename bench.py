@@ -48,6 +48,7 @@ def parse():
     p.add_argument("--ilp", type=int, default=2, help="32-row groups per warp step")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample duration")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--skip-full", action="store_true", help="skip the full-scan (early_abandon=0) comparison loops")
     p.add_argument("--verify", action="store_true",
                    help="rank 0 also searches the whole database on its GPU and checks the merged result bit-exactly")
     return p.parse_args()
@@ -144,24 +145,8 @@ def build_workload(args, rank: int, world: int):
 
 
 def gpu_encoder():
-    """Bit-exact PQ encode on the GPU (vk_encode_device), in 1M-row slices."""
-    def enc(cent, x):
-        import torch
-
-        from veckern_b200 import _native as N
-        m, _, dsub = cent.shape
-        out = np.empty((x.shape[0], m), np.uint8)
-        dev = torch.cuda.current_device()
-        step = 1 << 20
-        for a in range(0, x.shape[0], step):
-            xs = torch.from_numpy(np.ascontiguousarray(x[a:a + step])).cuda()
-            cs = torch.empty((xs.shape[0], m), dtype=torch.uint8, device="cuda")
-            N.check(N.lib().vk_encode_device(dev, N.ptr(np.ascontiguousarray(cent)), m, dsub, N.ptr(xs),
-                                             xs.shape[0], N.ptr(cs), torch.cuda.current_stream().cuda_stream),
-                    "encode")
-            out[a:a + xs.shape[0]] = cs.cpu().numpy()
-        return out
-    return enc
+    from veckern_b200.data import gpu_encoder as enc
+    return enc()
 
 
 # ------------------------------------------------------------------------------------------------ reference arm
@@ -283,19 +268,19 @@ def run_ours(args):
 
     # ---- the same steps with early abandoning off (full scan of every (query, row, sub-space) lookup)
     full_tuning = Tuning(queries_per_block=args.qpb, vectors_per_step=args.ilp, early_abandon=False)
-    for _ in range(args.warmup):
+    for _ in range(0 if args.skip_full else args.warmup):
         step_device(full_tuning)
     torch.cuda.synchronize()
     ev_full = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(args.steps)]
-    for i in range(args.steps):
+    for i in range(0 if args.skip_full else args.steps):
         flush.zero_()
         ev_full[i][0].record(stream)
         step_device(full_tuning)
         ev_full[i][1].record(stream)
     torch.cuda.synchronize()
     s.sync(stream)
-    full_ms = sum(a.elapsed_time(b) for a, b in ev_full)
+    full_ms = float("nan") if args.skip_full else sum(a.elapsed_time(b) for a, b in ev_full)
 
     # ---- e2e: the host-buffer C-ABI call (vk_search), rank-local; N > 1 adds gather + merge + result copy
     h_q = torch.from_numpy(w.queries).pin_memory().numpy()
@@ -324,8 +309,8 @@ def run_ours(args):
             sel_ms.append(t.select_ms)
     # scan-kernel duration of the full scan, from the same stage events
     s.set_tuning(full_tuning)
-    full_scan_ms = []
-    for i in range(args.warmup + args.steps):
+    full_scan_ms = [float("nan")] if args.skip_full else []
+    for i in range(0 if args.skip_full else args.warmup + args.steps):
         flush.zero_()
         _, t = s.search(h_q, k, out=h_out)
         if i >= args.warmup:
@@ -432,6 +417,20 @@ def cpu_baseline(args, w, spec):
     if int(os.environ.get("WORLD_SIZE", 1)) > 1:
         return None
     cores = os.cpu_count() or 1
+    if w.codes is None:  # generated database: the C port streams host-regenerated codes for one query
+        from veckern_b200 import data
+        P = oracle.port()
+        lut = P.compute_lut(w.centroids, w.queries[:1])
+        n = spec["n"]
+        rows = min(n, int(args.cpu_seconds * 4e6))  # bounded sample of the database (~args.cpu_seconds)
+        block = 1 << 22
+        t0 = time.perf_counter()
+        P.stream_search(lut, ((data.gen_codes(spec["code_seed"], w.cdf, a, min(block, rows - a)), a)
+                              for a in range(0, rows, block)), spec["k"], cores)
+        dt = time.perf_counter() - t0
+        return {"value": round(rows / n / dt, 4), "unit": "queries/s", "cores": cores, "kind": "port",
+                "sample": f"1 query over the first {rows:,} of {n:,} rows (codes regenerated on the host, "
+                          f"{dt:.1f} s), scaled to the full database"}
     kind = "reference" if oracle.ref_available() else "port"
     if kind == "reference":
         R = oracle.ref()

@@ -43,6 +43,10 @@ int vk_host_gen_cdf(uint64_t seed, int clusters, int m, double alpha, uint32_t* 
 int vk_host_gen_codes(uint64_t seed, const uint32_t* cdf, int clusters, int m, int64_t row0, int64_t n,
                       uint8_t* codes);
 
+/* the listed rows (count of them, any order) of the generated code database (row-major count x m) */
+int vk_host_gen_codes_rows(uint64_t seed, const uint32_t* cdf, int clusters, int m, const int64_t* rows,
+                           int64_t count, uint8_t* codes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -91,6 +91,7 @@ HOST_ABI = {
     "vk_host_gen_mixture": (C.c_int, [_u64, C.c_int, C.c_float, _u64, _i64, _i64, C.c_int, _vp]),
     "vk_host_gen_cdf": (C.c_int, [_u64, C.c_int, C.c_int, C.c_double, _vp]),
     "vk_host_gen_codes": (C.c_int, [_u64, _vp, C.c_int, C.c_int, _i64, _i64, _vp]),
+    "vk_host_gen_codes_rows": (C.c_int, [_u64, _vp, C.c_int, C.c_int, _vp, _i64, _vp]),
 }
 
 _lib = None

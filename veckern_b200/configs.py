@@ -20,6 +20,8 @@ import numpy as np
 
 from . import data
 
+SLICE_ROWS = 2_000_000  # rows generated and encoded at a time for large databases
+
 SPECS = {
     "c0": dict(kind="normal", n=100_000, d=128, m=16, nq=100, k=10, data_seed=0, pq_seed=1, pq_iters=0,
                query_seed=2),
@@ -79,10 +81,23 @@ def make(name: str, *, n: int | None = None, m: int | None = None, nq: int | Non
         train = x
         x = x[lo:hi]
     else:
-        x = data.gen_mixture(s["mix_seed"], s["mix_seed"], hi - lo, d, row0=lo)
         q = data.gen_mixture(s["mix_seed"], s["query_seed"], s["nq"], d)
         t = min(s["train_rows"], s["n"])
-        train = x[:t] if lo == 0 and hi >= t else data.gen_mixture(s["mix_seed"], s["mix_seed"], t, d)
+        train = data.gen_mixture(s["mix_seed"], s["mix_seed"], t, d)  # rows [0, t): the database's first rows
+        cent = data.pq_train(train, s["m"], s["pq_iters"], s["pq_seed"])
+        enc = encode or data.pq_encode
+        if keep_base or hi - lo <= SLICE_ROWS:
+            x = data.gen_mixture(s["mix_seed"], s["mix_seed"], hi - lo, d, row0=lo)
+            codes = enc(cent, x)
+        else:  # large databases: generate and encode slice by slice, keeping only the codes
+            x = None
+            codes = np.empty((hi - lo, s["m"]), np.uint8)
+            for a in range(lo, hi, SLICE_ROWS):
+                b = min(hi, a + SLICE_ROWS)
+                codes[a - lo:b - lo] = enc(cent, data.gen_mixture(s["mix_seed"], s["mix_seed"], b - a, d, row0=a))
+        w = Workload(name, s, cent, q, codes=codes, base=x if keep_base else None)
+        w.extra["row0"] = lo
+        return w
     cent = data.pq_train(train, s["m"], s["pq_iters"], s["pq_seed"])
     codes = (encode or data.pq_encode)(cent, x)
     w = Workload(name, s, cent, q, codes=codes, base=x if keep_base else None)

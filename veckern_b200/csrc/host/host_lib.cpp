@@ -262,4 +262,15 @@ int vk_host_gen_codes(uint64_t seed, const uint32_t* cdf, int clusters, int m, i
     return 0;
 }
 
+int vk_host_gen_codes_rows(uint64_t seed, const uint32_t* cdf, int clusters, int m, const int64_t* rows,
+                           int64_t count, uint8_t* codes) {
+    if (!cdf || !codes || !rows || clusters <= 0 || m <= 0 || count < 0) return -1;
+    const uint64_t key = vk::mix64(seed);
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < count; ++r)
+        for (int s = 0; s < m; ++s)
+            codes[r * m + s] = rows[r] < 0 ? 0 : (uint8_t)vk::gen_code(key, (uint64_t)rows[r], s, cdf, clusters, m);
+    return 0;
+}
+
 }  // extern "C"

@@ -75,3 +75,36 @@ def gen_codes(seed: int, cdf: np.ndarray, row0: int, n: int) -> np.ndarray:
     out = np.empty((n, m), np.uint8)
     _ok(host().vk_host_gen_codes(seed, ptr(cdf), clusters, m, row0, n, ptr(out)), "gen_codes")
     return out
+
+
+def gen_codes_rows(seed: int, cdf: np.ndarray, rows) -> np.ndarray:
+    """The listed rows of the generated code database (any order; negative rows give zeros)."""
+    cdf = np.ascontiguousarray(cdf, np.uint32)
+    rows = np.ascontiguousarray(rows, np.int64).ravel()
+    clusters, m, _ = cdf.shape
+    out = np.empty((rows.shape[0], m), np.uint8)
+    _ok(host().vk_host_gen_codes_rows(seed, ptr(cdf), clusters, m, ptr(rows), rows.shape[0], ptr(out)),
+        "gen_codes_rows")
+    return out
+
+
+def gpu_encoder(device: int | None = None):
+    """encode(centroids, x) -> codes on the GPU (vk_encode_device: bit-exact nearest centroid), 1M rows at a time."""
+    def enc(cent, x):
+        import torch
+
+        from ._native import check, lib
+        cent = np.ascontiguousarray(cent, np.float32)
+        m, _, dsub = cent.shape
+        dev = torch.cuda.current_device() if device is None else device
+        out = np.empty((x.shape[0], m), np.uint8)
+        step = 1 << 20
+        with torch.cuda.device(dev):
+            for a in range(0, x.shape[0], step):
+                xs = torch.from_numpy(np.ascontiguousarray(x[a:a + step])).cuda()
+                cs = torch.empty((xs.shape[0], m), dtype=torch.uint8, device="cuda")
+                check(lib().vk_encode_device(dev, ptr(cent), m, dsub, ptr(xs), xs.shape[0], ptr(cs),
+                                             torch.cuda.current_stream().cuda_stream), "encode")
+                out[a:a + xs.shape[0]] = cs.cpu().numpy()
+        return out
+    return enc
