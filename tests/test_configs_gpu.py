@@ -84,7 +84,7 @@ def _generated_checks(port, name, nq, ks, oracle_queries, split):
             parts.append(sh.search(w.queries, k)[0].view(np.int64).copy())
     gathered = torch.from_numpy(np.stack(parts)).cuda()  # [shard][q][k]
     merged = torch.empty((nq, k), dtype=torch.int64, device="cuda")
-    merge_topk_device(0, gathered, nq, split, k, k, k, nq * k, k, merged)
+    merge_topk_device(0, gathered, nq, split, k, k, nq * k, k, merged)  # [shard][q][k]: query stride k
     torch.cuda.synchronize()
     assert np.array_equal(merged.cpu().numpy(), results[k].view(np.int64)), f"{name}: {split} merged shards differ"
     # sampled queries against the oracle over the host-regenerated database
