@@ -183,9 +183,11 @@ __device__ __forceinline__ uint32_t code_byte(const uint4& v, int b) { return (w
 //   and finished 32 at a time, each lane dropping out as soon as its sum exceeds T_q; otherwise the whole tile
 //   is finished with the Q-wide lookups. Results are unchanged.
 // MT: m when it is 16, 32 or 64 (fully unrolled sub-space loop), 0 for any other m.
-// Two blocks share an SM whenever the group's LUT leaves room for that, so registers are capped at 128.
+// Block shape: two blocks of 8 warps share an SM when the group's LUT is at most 80 KB; a larger LUT leaves room
+// for one block, which then has 16 warps. Either way 16 warps per SM, registers capped at 128.
+__host__ __device__ constexpr int scan_warps(int Q, int MT) { return Q * (MT ? MT : 16) * KSUB * 4 <= 80 * 1024 ? 8 : 16; }
 template <int Q, int MT>
-constexpr int scan_min_blocks() { return Q * (MT ? MT : 16) * KSUB * 4 <= 80 * 1024 ? 2 : 1; }
+constexpr int scan_min_blocks() { return scan_warps(Q, MT) == 8 ? 2 : 1; }
 
 template <int Q, int MT, int ILP, int S, int NW, bool PRUNE>
 __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel(const ScanArgs a) {

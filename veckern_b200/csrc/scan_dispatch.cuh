@@ -1,11 +1,9 @@
-// Instantiation table of scan_kernel<Q, MT, ILP, S, NW, PRUNE>. Each Q lives in its own translation unit
+// Instantiation table of scan_kernel<Q, MT, ILP, S, NW = scan_warps(Q, MT), PRUNE>. Each Q lives in its own translation unit
 // (scan_q{1,2,4,8}.cu) so nvcc compiles them in parallel.
 #pragma once
 #include "kernels.cuh"
 
 namespace vk {
-
-constexpr int kScanWarps = 8;  // NW: warps per block (256 threads)
 
 // Returns the kernel for (mt in {16, 32, 64, 0}, ilp in {1, 2, 4}, s in {1, 2, 4}, prune); nullptr if there is
 // none (the pruned scan exists for mt in {16, 32, 64} and ilp in {1, 2}).
@@ -14,7 +12,7 @@ const void* scan_kernel_for(int mt, int ilp, int s, bool prune);
 
 #define VK_SCAN_CASE(Q, MT, ILP, S, P)            \
     case (P) * 10000 + MT * 100 + ILP * 10 + S: \
-        return reinterpret_cast<const void*>(&scan_kernel<Q, MT, ILP, S, kScanWarps, P>);
+        return reinterpret_cast<const void*>(&scan_kernel<Q, MT, ILP, S, scan_warps(Q, MT), P>);
 #define VK_SCAN_CASES_S(Q, MT, ILP, P) VK_SCAN_CASE(Q, MT, ILP, 1, P) VK_SCAN_CASE(Q, MT, ILP, 2, P) VK_SCAN_CASE(Q, MT, ILP, 4, P)
 #define VK_SCAN_CASES_MT(Q, MT) \
     VK_SCAN_CASES_S(Q, MT, 1, false) VK_SCAN_CASES_S(Q, MT, 2, false) VK_SCAN_CASES_S(Q, MT, 4, false)

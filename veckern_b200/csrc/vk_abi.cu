@@ -182,8 +182,6 @@ struct Plan {
 // ILP and the ring depth, then the chunk count with a wave model over the occupancy API's resident blocks:
 // time ~ ceil(items / resident) * (rows per chunk + a LUT-load overhead), minimised over the chunk count.
 int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan& p) {
-    const int nw = vk::kScanWarps;
-    p.threads = nw * 32;
     p.S = s_for_k(k);
     p.mt = (ix->m == 16 || ix->m == 32 || ix->m == 64) ? ix->m : 0;
     // Exact early abandoning: specialised for m in {16, 32, 64}; its compaction queue holds 1 or 2 row groups.
@@ -195,9 +193,11 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     const int ilp_req = p.prune ? std::min(t.vectors_per_step, 2) : t.vectors_per_step;
     p.ilp = ilp_req;
     p.stages = kStagesMax;
-    auto slots = [&](int q) { return (uint32_t)q * nw * k * 8u <= 16384u ? q : 1; };  // parallel item merges
+    // warps per block as the kernel is instantiated (vk::scan_warps); the generic-m kernel uses its table size
+    auto warps = [&](int q) { return vk::scan_warps(q, p.mt); };
+    auto slots = [&](int q) { return (uint32_t)q * warps(q) * k * 8u <= 16384u ? q : 1; };  // parallel merges
     auto fits = [&](int q, int ilp, int st) {
-        return vk::scan_smem_plan(q, ix->m, ix->W, ilp, nw, st, k, p.prune, slots(q)).total <=
+        return vk::scan_smem_plan(q, ix->m, ix->W, ilp, warps(q), st, k, p.prune, slots(q)).total <=
                (uint32_t)ix->smem_optin;
     };
     for (;;) {
@@ -206,9 +206,11 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
         if (p.ilp > 1) { p.ilp /= 2; p.stages = kStagesMax; continue; }
         if (Q > 1) { Q /= 2; p.ilp = ilp_req; p.stages = kStagesMax; continue; }
         return fail(VK_ERR_INVALID, "LUT does not fit in shared memory (m = %d needs %u bytes, device allows %d)",
-                    ix->m, vk::scan_smem_plan(1, ix->m, ix->W, 1, nw, 2, k, p.prune, 1).total, ix->smem_optin);
+                    ix->m, vk::scan_smem_plan(1, ix->m, ix->W, 1, warps(1), 2, k, p.prune, 1).total, ix->smem_optin);
     }
     p.Q = Q;
+    const int nw = warps(Q);
+    p.threads = nw * 32;
     p.fn = scan_kernel_ptr(Q, p.mt, p.ilp, p.S, p.prune);
     if (!p.fn) return fail(VK_ERR_UNSUPPORTED, "no scan kernel for Q=%d m=%d ilp=%d", Q, ix->m, p.ilp);
     p.merge_slots = slots(Q);
