@@ -44,7 +44,7 @@ def parse():
     p.add_argument("--n", type=int, default=None)
     p.add_argument("--nq", type=int, default=None)
     p.add_argument("--k", type=int, default=None)
-    p.add_argument("--qpb", type=int, default=4, help="queries per block (Q)")
+    p.add_argument("--qpb", type=int, default=8, help="queries per block (Q; reduced when the LUTs do not fit)")
     p.add_argument("--ilp", type=int, default=2, help="32-row groups per warp step")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample duration")
     p.add_argument("--no-cpu-baseline", action="store_true")

@@ -11,6 +11,26 @@
 
 namespace vk {
 
+// Compile-time loop: f(Int<i>) for i = 0 .. N-1. Arrays indexed by i keep constant indices (and stay in registers)
+// however large the loop body gets, where `#pragma unroll` is only a request (nvcc left the k = 100 lists' loops
+// rolled and moved the lists to local memory).
+template <int I>
+struct Int {
+    static constexpr int value = I;
+    __host__ __device__ constexpr operator int() const { return I; }
+};
+template <int I, int N, class F>
+__device__ __forceinline__ void static_for_impl(F&& f) {
+    if constexpr (I < N) {
+        f(Int<I>{});
+        static_for_impl<I + 1, N>(f);
+    }
+}
+template <int N, class F>
+__device__ __forceinline__ void static_for(F&& f) {
+    static_for_impl<0, N>(f);
+}
+
 template <int S>
 struct WarpTopK {
     float d[S];
@@ -19,11 +39,10 @@ struct WarpTopK {
     int32_t thr_i;
 
     __device__ __forceinline__ void init() {
-#pragma unroll
-        for (int r = 0; r < S; ++r) {
+        static_for<S>([&](auto r) {
             d[r] = __int_as_float(0x7f800000);  // +inf
             id[r] = SENTINEL_ID;
-        }
+        });
         thr_d = __int_as_float(0x7f800000);
         thr_i = SENTINEL_ID;
     }
@@ -34,12 +53,10 @@ struct WarpTopK {
     __device__ __forceinline__ void insert(float x, int32_t xi, int k) {
         const int lane = threadIdx.x & (WARP - 1);
         int pos = 0;
-#pragma unroll
-        for (int r = 0; r < S; ++r) pos += __popc(__ballot_sync(FULL, nb_less(d[r], id[r], x, xi)));
+        static_for<S>([&](auto r) { pos += __popc(__ballot_sync(FULL, nb_less(d[r], id[r], x, xi))); });
         float carry_d = x;
         int32_t carry_i = xi;
-#pragma unroll
-        for (int r = 0; r < S; ++r) {
+        static_for<S>([&](auto r) {
             float up_d = __shfl_up_sync(FULL, d[r], 1);
             int32_t up_i = __shfl_up_sync(FULL, id[r], 1);
             const float last_d = __shfl_sync(FULL, d[r], WARP - 1);
@@ -58,16 +75,16 @@ struct WarpTopK {
             }
             carry_d = last_d;
             carry_i = last_i;
-        }
+        });
         const int t = k - 1;
         float td = d[0];
         int32_t ti = id[0];
-#pragma unroll
-        for (int r = 1; r < S; ++r)
-            if ((t >> 5) == r) {
+        static_for<S>([&](auto r) {
+            if (r > 0 && (t >> 5) == r) {
                 td = d[r];
                 ti = id[r];
             }
+        });
         thr_d = __shfl_sync(FULL, td, t & (WARP - 1));
         thr_i = __shfl_sync(FULL, ti, t & (WARP - 1));
     }
@@ -87,11 +104,10 @@ struct WarpTopK {
     // Writes entries 0 .. k-1 (ascending) as (dist, id) pairs.
     __device__ __forceinline__ void store(int2* out, int k) const {
         const int lane = threadIdx.x & (WARP - 1);
-#pragma unroll
-        for (int r = 0; r < S; ++r) {
+        static_for<S>([&](auto r) {
             const int e = r * WARP + lane;
             if (e < k) out[e] = make_int2(__float_as_int(d[r]), id[r]);
-        }
+        });
     }
 };
 
