@@ -159,6 +159,13 @@ int vk_compute_lut_device(vk_index_t* index, const float* d_queries, int64_t nq,
 int vk_merge_topk_device(int device, const vk_neighbor_t* d_in, int64_t nq, int lists, int k_in,
                          int64_t query_stride, int64_t list_stride, int k, vk_neighbor_t* d_out, void* stream);
 
+/* Replaces rerank_exact (src/cpu/cpu_ref.cpp:66-77) on the device: for each of nq queries (DEVICE, nq x d fp32),
+ * re-scores its r candidates (DEVICE, nq x r vk_neighbor_t; only the ids are read, ids < 0 are skipped) against
+ * the DEVICE base vectors (n x d fp32, row = id) with the exact l2sq and keeps the k best (1 <= k <= 128),
+ * ascending, padded with {+inf, -1}: identical to the reference's CPU re-rank. */
+int vk_rerank_device(int device, const float* d_base, int64_t n, int d, const float* d_queries, int64_t nq,
+                     const vk_neighbor_t* d_candidates, int r, int k, vk_neighbor_t* d_out, void* stream);
+
 /* Bit-exact PQ encode on the device (nearest centroid per sub-space under the reference's l2sq, first minimum
  * wins; src/cpu/pq.cpp:11-22, 71-76): DEVICE x (n x d fp32) -> DEVICE codes (n x m). */
 int vk_encode_device(int device, const float* centroids, int m, int dsub, const float* d_x, int64_t n,

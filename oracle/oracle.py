@@ -44,6 +44,7 @@ class Port:
                                      C.c_int]
         L.vko_topk_push_all.argtypes = [_f32p, _i32p, _i64, C.c_int, _f32p, _i32p]
         L.vko_merge_topk.argtypes = [_f32p, _i32p, C.c_int, C.c_int, _i64, C.c_int, _f32p, _i32p]
+        L.vko_rerank_exact.argtypes = [_f32p, C.c_int, _f32p, _i64, _i32p, C.c_int, C.c_int, _f32p, _i32p]
         L.vko_recall_at_k.argtypes = [_i32p, _i64, _i32p, _i64, _i64, C.c_int]
         L.vko_recall_at_k.restype = C.c_double
         L.vko_stream_create.argtypes = [_f32p, _i64, C.c_int, C.c_int]
@@ -106,6 +107,16 @@ class Port:
         self.lib.vko_merge_topk(d, ids, lists, k_in, nq, k, od, oi)
         return od, oi
 
+    def rerank_exact(self, base, queries, cand_ids, k):
+        base = _f32(base)
+        queries = _f32(queries)
+        cand_ids = np.ascontiguousarray(cand_ids, np.int32)
+        nq, r = cand_ids.shape
+        d = np.empty((nq, k), np.float32)
+        i = np.empty((nq, k), np.int32)
+        self.lib.vko_rerank_exact(base, base.shape[1], queries, nq, cand_ids, r, k, d, i)
+        return d, i
+
     def recall_at_k(self, found, truth, k):
         found = np.ascontiguousarray(found, np.int32)
         truth = np.ascontiguousarray(truth, np.int32)
@@ -149,6 +160,7 @@ class Ref:
         L.ref_adc_search.argtypes = [C.c_void_p, _u8p, _i64, _f32p, _i64, _i64, _f32p, _i32p]
         L.ref_exact_knn.argtypes = [_f32p, _i64, _f32p, _i64, _i64, _i64, _f32p, _i32p]
         L.ref_topk_push_all.argtypes = [_f32p, _i32p, _i64, _i64, _f32p, _i32p]
+        L.ref_rerank_exact.argtypes = [_f32p, _i64, _f32p, _i64, _i32p, _i64, _i64, _f32p, _i32p]
         L.ref_synthetic_clustered.argtypes = [_i64, _i64, _i64, C.c_uint64, _f32p]
 
     class PQ:
@@ -231,6 +243,16 @@ class Ref:
         d = np.empty(k, np.float32)
         i = np.empty(k, np.int32)
         self.lib.ref_topk_push_all(_f32(dists), np.ascontiguousarray(ids, np.int32), len(dists), k, d, i)
+        return d, i
+
+    def rerank_exact(self, base, queries, cand_ids, k):
+        base = _f32(base)
+        queries = _f32(queries)
+        cand_ids = np.ascontiguousarray(cand_ids, np.int32)
+        nq, r = cand_ids.shape
+        d = np.empty((nq, k), np.float32)
+        i = np.empty((nq, k), np.int32)
+        self.lib.ref_rerank_exact(base, base.shape[1], queries, nq, cand_ids, r, k, d, i)
         return d, i
 
     def synthetic_clustered(self, n, d, clusters, seed):

@@ -71,6 +71,13 @@ void ref_exact_knn(const float* base, int64_t n, const float* queries, int64_t n
     veckern::exact_knn(base, n, queries, nq, d, k, out.data());
     split(out, out_d, out_i);
 }
+void ref_rerank_exact(const float* base, int64_t d, const float* queries, int64_t nq, const int32_t* cand_ids,
+                      int64_t r, int64_t k, float* out_d, int32_t* out_i) {
+    std::vector<Neighbor> cand(nq * r), out(nq * k);
+    for (int64_t j = 0; j < nq * r; ++j) cand[j] = {0.f, cand_ids[j]};
+    veckern::rerank_exact(base, d, queries, nq, cand.data(), r, k, out.data());
+    split(out, out_d, out_i);
+}
 void ref_topk_push_all(const float* dists, const int32_t* ids, int64_t count, int64_t k, float* out_d,
                        int32_t* out_i) {
     veckern::TopK top(k);

@@ -210,6 +210,28 @@ void vko_merge_topk(const float* d, const int32_t* ids, int lists, int k_in, int
     }
 }
 
+/* src/cpu/cpu_ref.cpp:66-77 (rerank_exact): candidates in order, id < 0 skipped, l2sq(query, base row). */
+void vko_rerank_exact(const float* base, int d, const float* queries, int64_t nq, const int32_t* cand_ids, int r,
+                      int k, float* out_d, int32_t* out_i) {
+#pragma omp parallel
+    {
+        float* hd = (float*)malloc(sizeof(float) * (size_t)(k > 0 ? k : 1));
+        int32_t* hi = (int32_t*)malloc(sizeof(int32_t) * (size_t)(k > 0 ? k : 1));
+#pragma omp for schedule(static)
+        for (int64_t q = 0; q < nq; ++q) {
+            topk_t t;
+            topk_init(&t, k, hd, hi);
+            for (int j = 0; j < r; ++j) {
+                const int32_t id = cand_ids[q * r + j];
+                if (id >= 0) topk_push(&t, l2sq(queries + q * d, base + (int64_t)id * d, d), id);
+            }
+            topk_write(&t, out_d + q * k, out_i + q * k);
+        }
+        free(hd);
+        free(hi);
+    }
+}
+
 /* src/cpu/cpu_ref.cpp:79-91 (recall_at_k), on id arrays. */
 double vko_recall_at_k(const int32_t* found, int64_t found_stride, const int32_t* truth, int64_t truth_stride,
                        int64_t nq, int k) {

@@ -46,6 +46,11 @@ void vko_topk_push_all(const float* dists, const int32_t* ids, int64_t count, in
 void vko_merge_topk(const float* d, const int32_t* ids, int lists, int k_in, int64_t nq, int k, float* out_d,
                     int32_t* out_i);
 
+/* Exact re-rank (src/cpu/cpu_ref.cpp:66-77): for each query, l2sq(query, base[id], d) of its r candidate ids
+ * (id < 0 skipped), pushed in candidate order through one bounded top-k of k. base: n x d, queries: nq x d. */
+void vko_rerank_exact(const float* base, int d, const float* queries, int64_t nq, const int32_t* cand_ids, int r,
+                      int k, float* out_d, int32_t* out_i);
+
 /* Mean |found[:k] ∩ truth[:k]| / k (src/cpu/cpu_ref.cpp:79-91). */
 double vko_recall_at_k(const int32_t* found, int64_t found_stride, const int32_t* truth, int64_t truth_stride,
                        int64_t nq, int k);

@@ -111,3 +111,26 @@ def test_port_matches_reference_random(port, seed, n, m, dsub, nq, k):
     rd, ri = R.adc_search(pq, codes, q, k)
     pd, pi = port.adc_search(pq.centroids, codes, q, k)
     assert_same_topk(pd, pi, rd, ri, "port vs reference")
+
+
+def test_rerank_matches_reference_fixture(port, golden):
+    """Exact re-rank of 100 PQ candidates (one padding entry) to 10, as the reference computes it."""
+    from veckern_b200 import data
+
+    g = golden("cpu_fixture")
+    base = data.synthetic_clustered(4000, 32, 20, 7)
+    d, i = port.rerank_exact(base, g["queries"], g["cand_i"], 10)
+    assert_same_topk(d, i, g["rr_d"], g["rr_i"], "rerank")
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="reference library not built here")
+def test_rerank_port_matches_reference_with_duplicates():
+    R = oracle.ref()
+    rng = np.random.default_rng(8)
+    base = rng.integers(-2, 3, size=(500, 16)).astype(np.float32)  # small integers: many exact ties
+    q = rng.integers(-2, 3, size=(7, 16)).astype(np.float32)
+    cand = rng.integers(-1, 500, size=(7, 90)).astype(np.int32)  # duplicates and padding on purpose
+    for k in (1, 10, 64, 128):
+        rd, ri = R.rerank_exact(base, q, cand, k)
+        pd, pi = oracle.port().rerank_exact(base, q, cand, k)
+        assert_same_topk(pd, pi, rd, ri, f"rerank k={k}")

@@ -306,3 +306,33 @@ def test_index_codes_roundtrip(golden):
     with PQSearcher(g["centroids"], g["codes"]) as s:
         assert np.array_equal(s.get_codes(), g["codes"])
         assert np.array_equal(s.get_codes(20_000, 11), g["codes"][20_000:])
+
+
+def test_rerank_kernel_matches_reference(golden, port):
+    """GPU exact re-rank == the reference's rerank_exact (fixture) and the oracle (duplicates, padding, ties)."""
+    import torch
+
+    from veckern_b200 import data, rerank_device
+
+    g = golden("cpu_fixture")
+    base = data.synthetic_clustered(4000, 32, 20, 7)
+
+    def gpu(base, q, cand_ids, k):
+        pairs = np.stack([np.zeros_like(cand_ids), cand_ids], axis=-1).astype(np.int32)
+        d_c = torch.from_numpy(np.ascontiguousarray(pairs)).cuda().view(torch.int64).reshape(cand_ids.shape)
+        d_out = torch.empty((q.shape[0], k), dtype=torch.int64, device="cuda")
+        rerank_device(0, torch.from_numpy(base).cuda(), torch.from_numpy(q).cuda(), d_c, k, d_out)
+        torch.cuda.synchronize()
+        o = d_out.cpu().numpy().view(np.int32).reshape(q.shape[0], k, 2)
+        return o[..., 0].view(np.float32), o[..., 1]
+
+    d, i = gpu(base, g["queries"], g["cand_i"], 10)
+    assert_same_topk(d, i, g["rr_d"], g["rr_i"], "rerank fixture")
+    rng = np.random.default_rng(8)
+    base = rng.integers(-2, 3, size=(500, 16)).astype(np.float32)
+    q = rng.integers(-2, 3, size=(37, 16)).astype(np.float32)
+    cand = rng.integers(-1, 500, size=(37, 90)).astype(np.int32)
+    for k in (1, 10, 64, 128):
+        ed, ei = port.rerank_exact(base, q, cand, k)
+        d, i = gpu(base, q, cand, k)
+        assert_same_topk(d, i, ed, ei, f"rerank k={k}")

@@ -6,4 +6,4 @@ include/veckern/gpu.hpp). This package is the Python host side over that ABI; it
 """
 from .searcher import (NEIGHBOR_DTYPE, DeviceInfo, LaunchShape, PQSearcher, ScanVariant, Timings, Tuning,  # noqa
                        VkError, device_info, device_result_split, empty_neighbors, is_fused, merge_topk_device,
-                       neighbors_split, variant_name)
+                       neighbors_split, rerank_device, variant_name)

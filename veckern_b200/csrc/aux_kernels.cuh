@@ -128,4 +128,53 @@ __global__ void __launch_bounds__(256) encode_kernel(const float* __restrict__ c
     codes[i * m + s] = (uint8_t)best;
 }
 
+// ------------------------------------------------------------------------------------------------ re-rank
+// Exact re-rank (the reference's rerank_exact, src/cpu/cpu_ref.cpp:66-77): one warp per query; lane l re-scores
+// candidates l, l + 32, ... with l2sq(query, base row) summed over j in order, each operation rounded on its own
+// (diff = q - b, acc += diff * diff; no FMA), and the warp keeps the k best (dist, id) in candidate order through
+// WarpTopK (same admission rule as the reference's heap, so duplicates and ties come out identically).
+// Candidate ids < 0 are skipped. The query row is staged in shared memory (block: 4 warps, 4 queries).
+template <int S>
+__global__ void __launch_bounds__(128) rerank_kernel(const float* __restrict__ base, int d,
+                                                     const float* __restrict__ queries, int64_t nq,
+                                                     const int2* __restrict__ cand, int r, int k,
+                                                     int2* __restrict__ out) {
+    extern __shared__ float sq[];  // [4][d]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t q = (int64_t)blockIdx.x * 4 + warp;
+    float* my_q = sq + warp * d;
+    if (q < nq)
+        for (int j = lane; j < d; j += 32) my_q[j] = queries[q * d + j];
+    __syncwarp();
+    if (q >= nq) return;  // warp-uniform
+    WarpTopK<S> top;
+    top.init();
+    for (int j0 = 0; j0 < r; j0 += 32) {
+        const int j = j0 + lane;
+        const int id = j < r ? cand[q * r + j].y : -1;
+        float acc = 0.f;
+        if (id >= 0) {
+            const float* b = base + (int64_t)id * d;
+            for (int t = 0; t < d; ++t) {
+                const float diff = __fsub_rn(my_q[t], b[t]);
+                acc = __fadd_rn(acc, __fmul_rn(diff, diff));
+            }
+        }
+        // candidates are pushed in candidate order: offer the 32 of this round one lane at a time, so ties and
+        // duplicates meet the list in the same order as the reference's loop
+        for (int src = 0; src < 32; ++src) {
+            const float x = __shfl_sync(FULL, acc, src);
+            const int xi = __shfl_sync(FULL, id, src);
+            if (xi >= 0 && top.admits(x, xi)) top.insert(x, xi, k);
+        }
+    }
+    static_for<S>([&](auto rr) {
+        const int e = rr * 32 + lane;
+        if (e < k) {
+            const bool pad = top.id[rr] == SENTINEL_ID;
+            out[q * k + e] = pad ? make_int2(0x7f800000, -1) : make_int2(__float_as_int(top.d[rr]), top.id[rr]);
+        }
+    });
+}
+
 }  // namespace vk

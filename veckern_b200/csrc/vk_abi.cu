@@ -225,9 +225,11 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     const int64_t tile_rows = 32 * p.ilp;
     const int64_t tiles = ix->n_pad / tile_rows;
     const int64_t max_chunks = std::max<int64_t>(1, tiles / (2 * nw));  // >= 2 tiles per warp per chunk
-    // The pruned scan tightens each query's bound as chunks complete: use enough chunks for that to pay off.
+    // The pruned scan tightens each query's bound as chunks complete: use enough chunks for that to pay off
+    // (up to 48), but keep chunks of at least 16K rows so that each item's LUT load stays amortised.
+    const int64_t prune_chunks = p.prune ? std::max<int64_t>(1, std::min<int64_t>(48, ix->n_pad / 16384)) : 1;
     const int64_t min_chunks =
-        std::min(max_chunks, std::max<int64_t>(ceil_div(ix->n_pad, kMaxRowsPerChunk), p.prune ? 48 : 1));
+        std::min(max_chunks, std::max<int64_t>(ceil_div(ix->n_pad, kMaxRowsPerChunk), prune_chunks));
     int64_t chunks = min_chunks;
     if (t.blocks_per_query > 0) {
         chunks = std::min<int64_t>(t.blocks_per_query, max_chunks);
@@ -746,6 +748,31 @@ int vk_merge_topk_device(int device, const vk_neighbor_t* d_in, int64_t nq, int 
         default: vk::merge_kernel<4><<<(unsigned)ceil_div(nq, 4), 128, 0, st>>>(in, nq, lists, k_in, query_stride, list_stride, k, o); break;
     }
     VK_TRY_CUDA(cudaGetLastError());
+    return VK_OK;
+}
+
+int vk_rerank_device(int device, const float* d_base, int64_t n, int d, const float* d_queries, int64_t nq,
+                     const vk_neighbor_t* d_candidates, int r, int k, vk_neighbor_t* d_out, void* stream) {
+    if (k < 1 || k > 128) return fail(VK_ERR_INVALID, "k must be in [1, 128]");
+    if (n < 0 || nq < 0 || r < 0 || d <= 0) return fail(VK_ERR_INVALID, "bad sizes");
+    if (nq == 0) return VK_OK;
+    if (!d_base || !d_queries || !d_out || (r > 0 && !d_candidates))
+        return fail(VK_ERR_INVALID, "pointers must not be NULL");
+    if ((size_t)4 * d * sizeof(float) > 48 * 1024) return fail(VK_ERR_UNSUPPORTED, "d = %d is too large", d);
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int2* c = reinterpret_cast<const int2*>(d_candidates);
+    int2* o = reinterpret_cast<int2*>(d_out);
+    const dim3 grid((unsigned)ceil_div(nq, 4));
+    const size_t smem = (size_t)4 * d * sizeof(float);
+    switch (s_for_k(k)) {
+        case 1: vk::rerank_kernel<1><<<grid, 128, smem, st>>>(d_base, d, d_queries, nq, c, r, k, o); break;
+        case 2: vk::rerank_kernel<2><<<grid, 128, smem, st>>>(d_base, d, d_queries, nq, c, r, k, o); break;
+        default: vk::rerank_kernel<4><<<grid, 128, smem, st>>>(d_base, d, d_queries, nq, c, r, k, o); break;
+    }
+    VK_TRY_CUDA(cudaGetLastError());
+    (void)n;
     return VK_OK;
 }
 

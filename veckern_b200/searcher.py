@@ -244,6 +244,14 @@ def merge_topk_device(device: int, d_in, nq: int, lists: int, k_in: int, query_s
                                      _stream_handle(stream)), "merge_topk")
 
 
-__all__ = ["ScanVariant", "Tuning", "Timings", "LaunchShape", "DeviceInfo", "PQSearcher", "VkError",
+def rerank_device(device: int, d_base, d_queries, d_candidates, k: int, d_out, stream=None) -> None:
+    """Exact re-rank on the GPU (the reference's rerank_exact): torch tensors d_base [n, d] f32, d_queries [nq, d]
+    f32, d_candidates [nq, r] int64 (dist, id) pairs (ids < 0 skipped), d_out [nq, k] int64 pairs."""
+    nq, r = d_candidates.shape
+    check(lib().vk_rerank_device(device, ptr(d_base), d_base.shape[0], d_base.shape[1], ptr(d_queries), nq,
+                                 ptr(d_candidates), r, k, ptr(d_out), _stream_handle(stream)), "rerank")
+
+
+__all__ = ["rerank_device", "ScanVariant", "Tuning", "Timings", "LaunchShape", "DeviceInfo", "PQSearcher", "VkError",
            "NEIGHBOR_DTYPE", "device_info", "variant_name", "is_fused", "neighbors_split", "empty_neighbors",
            "device_result_split", "merge_topk_device"]
