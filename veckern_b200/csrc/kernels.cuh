@@ -119,7 +119,7 @@ __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp,
 
 // Sub-spaces the pruned scan computes for every row before it tests rows against the bounds (phase A). Chosen
 // from the survival curves of partial sums: few (query, row) pairs get past ~5/16 of the sub-spaces.
-__host__ __device__ constexpr int prune_depth(int m) { return m <= 16 ? 6 : m <= 32 ? 10 : 20; }
+__host__ __device__ constexpr int prune_depth(int m) { return m <= 16 ? 8 : m <= 32 ? 12 : 20; }
 
 // One sub-space lookup for Q queries: acc[q] += LUT_q[s][c], rounded per add, in s order.
 template <int Q>
@@ -462,11 +462,13 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                         }
                     }
                     const int32_t id = (int32_t)(a.id_base + tile_row0 + r);
+                    if (__any_sync(FULL, live)) {  // usually every pair of the batch was abandoned
 #pragma unroll
-                    for (int qq = 0; qq < Q; ++qq) {
-                        if (__any_sync(FULL, live && q == qq)) {
-                            top[qq].offer(x, id, live && q == qq, a.k);
-                            bnd[qq] = fminf(bnd[qq], top[qq].thr_d);
+                        for (int qq = 0; qq < Q; ++qq) {
+                            if (__any_sync(FULL, live && q == qq)) {
+                                top[qq].offer(x, id, live && q == qq, a.k);
+                                bnd[qq] = fminf(bnd[qq], top[qq].thr_d);
+                            }
                         }
                     }
                 }
