@@ -117,9 +117,15 @@ __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp,
     return p;
 }
 
-// Sub-spaces the pruned scan computes for every row before it tests rows against the bounds (phase A). Chosen
-// from the survival curves of partial sums: few (query, row) pairs get past ~5/16 of the sub-spaces.
-__host__ __device__ constexpr int prune_depth(int m) { return m <= 16 ? 8 : m <= 32 ? 12 : 20; }
+// Depth of phase A in the pruned scan: sub-spaces computed for every row before the rows are tested against the
+// bounds. A tile is first tested at prune_first(m); while more than 1/PRUNE_DEEPEN of its (row, query) pairs
+// survive, phase A goes two sub-spaces deeper, up to prune_last(m): below that share, finishing the survivors one
+// pair per lane costs less than two more Q-wide sub-spaces of every row. Survival curves of partial sums differ
+// between data sets (on the clustered SIFT-shaped mixture at m = 16, 0.15% of the pairs survive 8 sub-spaces; on
+// the Dirichlet-generated codes 72% survive 8, 20% survive 10 and 1.3% survive 12), hence the per-tile choice.
+__host__ __device__ constexpr int prune_first(int m) { return m <= 16 ? 8 : m <= 32 ? 12 : 24; }
+__host__ __device__ constexpr int prune_last(int m) { return m <= 16 ? 12 : m <= 32 ? 16 : 28; }
+constexpr int PRUNE_DEEPEN = 8;
 
 // One sub-space lookup for Q queries: acc[q] += LUT_q[s][c], rounded per add, in s order.
 template <int Q>
@@ -194,8 +200,9 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
     static_assert(!PRUNE || MT != 0, "the pruned scan is specialised for m = 16, 32, 64");
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int W_T = MT ? (MT + 15) / 16 : 0;
-    constexpr int SA = prune_depth(MT);
-    static_assert(!PRUNE || SA % 2 == 0, "phase B fetches sub-spaces in pairs inside one 16-byte word");
+    constexpr int SA = prune_first(MT), SAX = prune_last(MT);
+    static_assert(!PRUNE || (SA % 2 == 0 && SAX % 2 == 0 && SAX >= SA && SAX < MT),
+                  "phase A stops at even sub-spaces: phase B fetches sub-spaces in pairs inside one 16-byte word");
     const int m = MT ? MT : a.m;
     const int W = MT ? W_T : a.W;
     const ScanSmem plan = scan_smem_plan(Q, m, W, ILP, NW, a.stages, a.k, PRUNE, a.merge_slots);
@@ -359,15 +366,16 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
 #pragma unroll
                     for (int q = 0; q < Q; ++q) acc[u][q] = 0.f;
                 uint4 cv[ILP];
-#pragma unroll
-                for (int s = 0; s < SA; ++s) {
-                    if (s % 16 == 0) {
+                auto phase_a = [&](auto sc) {  // one sub-space (a compile-time constant) of every row
+                    constexpr int s = decltype(sc)::value;
+                    if constexpr (s % 16 == 0) {
 #pragma unroll
                         for (int u = 0; u < ILP; ++u) cv[u] = st[(u * W_T + s / 16) * 32 + lane];
                     }
 #pragma unroll
                     for (int u = 0; u < ILP; ++u) lookup_add<Q>(lut_smem, MT, s, code_byte(cv[u], s % 16), acc[u]);
-                }
+                };
+                static_for<SA>(phase_a);
                 float bnd[Q];
 #pragma unroll
                 for (int q = 0; q < Q; ++q) {
@@ -378,29 +386,36 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                 // ---- surviving (row, query) pairs
                 unsigned masks[ILP][Q];
                 int total = 0;
+                auto vote = [&]() {
+                    total = 0;
 #pragma unroll
-                for (int u = 0; u < ILP; ++u) {
-                    const bool valid = tile_row0 + u * 32 + lane < a.n;
+                    for (int u = 0; u < ILP; ++u) {
+                        const bool valid = tile_row0 + u * 32 + lane < a.n;
 #pragma unroll
-                    for (int q = 0; q < Q; ++q) {
-                        masks[u][q] = __ballot_sync(FULL, valid && !(acc[u][q] > bnd[q]));
-                        total += __popc(masks[u][q]);
+                        for (int q = 0; q < Q; ++q) {
+                            masks[u][q] = __ballot_sync(FULL, valid && !(acc[u][q] > bnd[q]));
+                            total += __popc(masks[u][q]);
+                        }
                     }
-                }
+                };
+                vote();
+                // ---- deeper phase A while many pairs survive (warp-uniform: total comes from ballots)
+                int dep = SA;
+                static_for<(SAX - SA) / 2>([&](auto e) {
+                    constexpr int s0 = SA + 2 * decltype(e)::value;
+                    if (dep == s0 && total * PRUNE_DEEPEN > 32 * ILP * Q) {
+                        phase_a(Int<s0>{});
+                        phase_a(Int<s0 + 1>{});
+                        dep = s0 + 2;
+                        vote();
+                    }
+                });
                 int cnt = 0;
                 if (2 * total > 32 * ILP * Q) {
-                    // Most pairs survive (no tight bound yet): finishing every row with the Q-wide lookups of the
-                    // full scan is cheaper than finishing pairs one query per lane.
-#pragma unroll
-                    for (int s = SA; s < MT; ++s) {
-                        if (s % 16 == 0) {
-#pragma unroll
-                            for (int u = 0; u < ILP; ++u) cv[u] = st[(u * W_T + s / 16) * 32 + lane];
-                        }
-#pragma unroll
-                        for (int u = 0; u < ILP; ++u)
-                            lookup_add<Q>(lut_smem, MT, s, code_byte(cv[u], s % 16), acc[u]);
-                    }
+                    // Most pairs survive (no tight bound yet), which the deepening above leaves possible only at
+                    // dep == SAX: finishing every row with the Q-wide lookups of the full scan is cheaper than
+                    // finishing pairs one query per lane.
+                    static_for<MT - SAX>([&](auto e) { phase_a(Int<SAX + decltype(e)::value>{}); });
                     bool any = false;
                     int32_t ids[ILP];
 #pragma unroll
@@ -428,49 +443,59 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                         }
                 }
                 __syncwarp();
-                // ---- phase B: finish the queued pairs 32 at a time, two sub-spaces per step, each lane dropping out
-                // as soon as its sum exceeds its query's bound
-                for (int base = 0; base < cnt; base += 32) {
-                    const int e = base + lane;
-                    bool live = e < cnt;
-                    const int2 ent = live ? my_queue[e] : make_int2(0, 0);
-                    float x = __int_as_float(ent.x);
-                    const int r = ent.y & 0xffff, q = ent.y >> 16;
-                    float bq = bnd[0];
+                // ---- phase B: finish the queued pairs 32 at a time from sub-space D = dep, two sub-spaces per step,
+                // each lane dropping out as soon as its sum exceeds its query's bound. One copy per depth, so that
+                // every sub-space index stays a compile-time constant.
+                auto phase_b = [&](auto dc) {
+                    constexpr int D = decltype(dc)::value;
+                    for (int base = 0; base < cnt; base += 32) {
+                        const int e = base + lane;
+                        bool live = e < cnt;
+                        const int2 ent = live ? my_queue[e] : make_int2(0, 0);
+                        float x = __int_as_float(ent.x);
+                        const int r = ent.y & 0xffff, q = ent.y >> 16;
+                        float bq = bnd[0];
 #pragma unroll
-                    for (int qq = 1; qq < Q; ++qq)
-                        if (q == qq) bq = bnd[qq];
-                    const unsigned char* lq = lut_smem + lut_query_base<Q>(q, MT);
-                    const uint4* rowp = st + (r >> 5) * W_T * 32 + (r & 31);
-                    uint4 cw = make_uint4(0, 0, 0, 0);
+                        for (int qq = 1; qq < Q; ++qq)
+                            if (q == qq) bq = bnd[qq];
+                        const unsigned char* lq = lut_smem + lut_query_base<Q>(q, MT);
+                        const uint4* rowp = st + (r >> 5) * W_T * 32 + (r & 31);
+                        uint4 cw = make_uint4(0, 0, 0, 0);
 #pragma unroll
-                    for (int s = SA; s < MT; s += 2) {
-                        if (s == SA || s % 16 == 0) {
-                            if (!__any_sync(FULL, live)) break;
-                            if (live) cw = rowp[(s / 16) * 32];
-                        } else if ((s - SA) % 4 == 0 && !__any_sync(FULL, live)) {
-                            break;
+                        for (int s = D; s < MT; s += 2) {
+                            if (s == D || s % 16 == 0) {
+                                if (!__any_sync(FULL, live)) break;
+                                if (live) cw = rowp[(s / 16) * 32];
+                            } else if ((s - D) % 4 == 0 && !__any_sync(FULL, live)) {
+                                break;
+                            }
+                            if (live) {
+                                const uint32_t c0 = code_byte(cw, s % 16), c1 = code_byte(cw, (s + 1) % 16);
+                                const float v0 = *reinterpret_cast<const float*>(lq + ((uint32_t)s * KSUB + c0) * lut_entry_bytes<Q>());
+                                const float v1 = *reinterpret_cast<const float*>(lq + ((uint32_t)(s + 1) * KSUB + c1) * lut_entry_bytes<Q>());
+                                x = __fadd_rn(x, v0);
+                                live = !(x > bq);
+                                x = __fadd_rn(x, v1);
+                                live = live && !(x > bq);
+                            }
                         }
-                        if (live) {
-                            const uint32_t c0 = code_byte(cw, s % 16), c1 = code_byte(cw, (s + 1) % 16);
-                            const float v0 = *reinterpret_cast<const float*>(lq + ((uint32_t)s * KSUB + c0) * lut_entry_bytes<Q>());
-                            const float v1 = *reinterpret_cast<const float*>(lq + ((uint32_t)(s + 1) * KSUB + c1) * lut_entry_bytes<Q>());
-                            x = __fadd_rn(x, v0);
-                            live = !(x > bq);
-                            x = __fadd_rn(x, v1);
-                            live = live && !(x > bq);
-                        }
-                    }
-                    const int32_t id = (int32_t)(a.id_base + tile_row0 + r);
-                    if (__any_sync(FULL, live)) {  // usually every pair of the batch was abandoned
+                        const int32_t id = (int32_t)(a.id_base + tile_row0 + r);
+                        if (__any_sync(FULL, live)) {  // usually every pair of the batch was abandoned
 #pragma unroll
-                        for (int qq = 0; qq < Q; ++qq) {
-                            if (__any_sync(FULL, live && q == qq)) {
-                                top[qq].offer(x, id, live && q == qq, a.k);
-                                bnd[qq] = fminf(bnd[qq], top[qq].thr_d);
+                            for (int qq = 0; qq < Q; ++qq) {
+                                if (__any_sync(FULL, live && q == qq)) {
+                                    top[qq].offer(x, id, live && q == qq, a.k);
+                                    bnd[qq] = fminf(bnd[qq], top[qq].thr_d);
+                                }
                             }
                         }
                     }
+                };
+                if (cnt > 0) {
+                    static_for<(SAX - SA) / 2 + 1>([&](auto e) {
+                        constexpr int D = SA + 2 * decltype(e)::value;
+                        if (dep == D) phase_b(Int<D>{});
+                    });
                 }
                 __syncwarp();  // the queue and the stage slot are free again
                 if (lane == 0) refill();
