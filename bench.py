@@ -46,6 +46,7 @@ def parse():
     p.add_argument("--k", type=int, default=None)
     p.add_argument("--qpb", type=int, default=8, help="queries per block (Q; reduced when the LUTs do not fit)")
     p.add_argument("--ilp", type=int, default=2, help="32-row groups per warp step")
+    p.add_argument("--bpq", type=int, default=0, help="vector chunks per query group (0: planned by the library)")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample duration")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--skip-full", action="store_true", help="skip the full-scan (early_abandon=0) comparison loops")
@@ -61,17 +62,65 @@ def rank_info():
 
 
 class ClockSampler:
-    """nvidia-smi clocks + throttle reasons sampled every 100 ms during the timed region."""
+    """SM clock, power and clock-event (throttle) reasons sampled every 5 ms during the timed region.
+
+    Reads NVML in a background thread (read-only queries); the device is found by its UUID, so the sample follows
+    the CUDA device whatever CUDA_VISIBLE_DEVICES says. Without NVML it falls back to `nvidia-smi -lms 100`."""
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, device: int):
+    def __init__(self, device: int, period_s: float = 0.005):
         self.device = device
+        self.period = period_s
+        self.rows = []  # (sm_mhz, max_mhz, power_w, reasons)
         self.proc = None
+        self.thread = None
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"vk_clocks_{os.getpid()}.csv"
 
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device)
+
     def start(self):
+        import threading
+        try:
+            nv, h = self._nvml_handle()
+            bits = {name: getattr(nv, "nvmlClocksEventReason" + key, getattr(nv, "nvmlClocksThrottleReason" + key))
+                    for name, key in zip(self.NAMES, ("HwSlowdown", "HwThermalSlowdown", "SwThermalSlowdown",
+                                                      "SwPowerCap"))}
+            reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons",
+                                 getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+            max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self._stop = threading.Event()
+
+            def sample():
+                mask = reasons_fn(h)
+                self.rows.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)), max_mhz,
+                                  nv.nvmlDeviceGetPowerUsage(h) / 1e3, [n for n, b in bits.items() if mask & b]))
+
+            def loop():
+                while not self._stop.is_set():
+                    try:
+                        sample()
+                    except Exception:
+                        pass
+                    self._stop.wait(self.period)
+
+            sample()  # fail here, not in the thread, if NVML cannot be read
+            self.rows.clear()
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],
@@ -80,28 +129,33 @@ class ClockSampler:
             self.proc = None
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.send_signal(signal.SIGTERM)
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        rows = []
-        for line in self.path.read_text().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) >= 9:
-                rows.append(f)
-        self.path.unlink(missing_ok=True)
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
+            rows = self.rows
+            source = "nvml"
+        elif self.proc is not None:
+            self.proc.send_signal(signal.SIGTERM)
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            rows = []
+            for line in self.path.read_text().splitlines():
+                f = [x.strip() for x in line.split(",")]
+                if len(f) >= 9 and f[1].replace(".", "").isdigit():
+                    rows.append((float(f[1]), float(f[2]) if f[2].replace(".", "").isdigit() else float("nan"),
+                                 float(f[3]) if f[3].replace(".", "").isdigit() else float("nan"),
+                                 [self.NAMES[i] for i in range(4) if f[5 + i].lower() == "active"]))
+            self.path.unlink(missing_ok=True)
+            source = "nvidia-smi"
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source (NVML, nvidia-smi)"]}
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows),
-                "power_w_max": max((float(r[3]) for r in rows if r[3].replace(".", "").isdigit()), default=None)}
+        return {"sm_mhz": float(np.median([r[0] for r in rows])), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted({x for r in rows for x in r[3]}), "samples": len(rows), "source": source,
+                "power_w_max": round(max(r[2] for r in rows), 1)}
 
 
 def lookup_wavefront_model(codes: np.ndarray, Q: int, sample_rows: int = 1 << 17) -> float:
@@ -215,7 +269,7 @@ def run_ours(args):
     spec, w, sh = build_workload(args, rank, world)
     n, m, nq, k = spec["n"], spec["m"], spec["nq"], spec["k"]
     lo, hi = sh.lo, sh.hi
-    tuning = Tuning(queries_per_block=args.qpb, vectors_per_step=args.ilp)
+    tuning = Tuning(queries_per_block=args.qpb, vectors_per_step=args.ilp, blocks_per_query=args.bpq)
     if w.codes is not None:
         s = PQSearcher(w.centroids, w.codes, device=local, id_base=lo)
     else:
@@ -267,7 +321,8 @@ def run_ours(args):
     dev_ms = sum(a.elapsed_time(b) for a, b in ev)
 
     # ---- the same steps with early abandoning off (full scan of every (query, row, sub-space) lookup)
-    full_tuning = Tuning(queries_per_block=args.qpb, vectors_per_step=args.ilp, early_abandon=False)
+    full_tuning = Tuning(queries_per_block=args.qpb, vectors_per_step=args.ilp, blocks_per_query=args.bpq,
+                         early_abandon=False)
     for _ in range(0 if args.skip_full else args.warmup):
         step_device(full_tuning)
     torch.cuda.synchronize()

@@ -11,8 +11,8 @@ namespace vk {
 // ------------------------------------------------------------------------------------------------ distances
 // Materialising ADC scan for PQSearcher::distances (src/cuda/searcher.cu:522-547): grid (bx, nq_batch),
 // block T; the query's [s][c] LUT in shared memory; dists[q][i] for every row i < n, same add order.
-__global__ void dist_kernel(const uint4* __restrict__ codes, const float* __restrict__ lut, int64_t n, int m,
-                            int W, float* __restrict__ out) {
+__global__ void dist_kernel(const uint4* __restrict__ codes, const uint8_t* __restrict__ perm,
+                            const float* __restrict__ lut, int64_t n, int m, int W, float* __restrict__ out) {
     extern __shared__ float slut[];
     const float* src = lut + (int64_t)blockIdx.y * m * KSUB;
     for (int t = threadIdx.x; t < m * KSUB; t += blockDim.x) slut[t] = src[t];
@@ -30,7 +30,7 @@ __global__ void dist_kernel(const uint4* __restrict__ codes, const float* __rest
                 acc = __fadd_rn(acc, slut[s * KSUB + c]);
             }
         }
-        out[(int64_t)blockIdx.y * n + i] = acc;
+        out[(int64_t)blockIdx.y * n + (i & ~(int64_t)(PLACE_WINDOW - 1)) + perm[i]] = acc;  // column = row id
     }
 }
 
@@ -57,15 +57,144 @@ __global__ void interleave_kernel(const uint8_t* __restrict__ rows, int64_t row0
     }
 }
 
-// Inverse of interleave_kernel for rows [first, first + count): row-major output (tests and tools).
-__global__ void deinterleave_kernel(const uint4* __restrict__ codes, int64_t first, int64_t count, int m, int W,
-                                    uint8_t* __restrict__ out) {
-    const int64_t total = count * m;
+// Inverse of interleave_kernel + place_rows_kernel for rows [first, first + count): row-major output (tests and
+// tools). One thread per (position, sub-space) of the placement windows covering the rows.
+__global__ void deinterleave_kernel(const uint4* __restrict__ codes, const uint8_t* __restrict__ perm, int64_t first,
+                                    int64_t count, int m, int W, uint8_t* __restrict__ out) {
+    const int64_t p0 = first & ~(int64_t)(PLACE_WINDOW - 1);
+    const int64_t total = ((first + count + PLACE_WINDOW - 1) / PLACE_WINDOW * PLACE_WINDOW - p0) * m;
     for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total; o += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = o / m, s = o - r * m;
-        const int64_t i = first + r;
+        const int64_t i = p0 + o / m, s = o % m;
+        const int64_t row = (i & ~(int64_t)(PLACE_WINDOW - 1)) + perm[i];
+        if (row < first || row >= first + count) continue;
         const uint4 v = codes[((i >> 5) * W + (s >> 4)) * 32 + (i & 31)];
-        out[o] = (uint8_t)((word_of(v, (int)(s & 15)) >> (8 * (s & 3))) & 0xffu);
+        out[(row - first) * m + s] = (uint8_t)((word_of(v, (int)(s & 15)) >> (8 * (s & 3))) & 0xffu);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ lane placement
+// Index build: reorders the rows of every whole window of PLACE_WINDOW rows (all positions < n; other windows and
+// m > 64 keep the identity) and records the order in perm. A warp's LUT fetch is served in phases of P lanes, P
+// bank groups each (P = 8: 16-byte entries, Q >= 4 layouts; P = 16: 8-byte entries, Q = 2): entry c of a sub-space
+// table lies in group c mod P. The cost of a placement is the sum over sub-spaces (weight w_s) and phases of the
+// largest number of the phase's rows whose codes share a group, i.e. the fetch's wavefronts when no two of those
+// rows hold the same code. Hill climbing: `steps` swaps of two positions in different phases, drawn from a
+// per-window counter-based sequence (deterministic layout), each kept when it does not raise the cost. Weights
+// follow the pruned scan: w = 20 for s < first_depth (phase A of every row), 6 for s < last_depth, 1 beyond.
+// One warp per window; lane l keeps the counts of sub-spaces l and l + 32.
+__host__ __device__ constexpr uint32_t place_warp_smem(int m, int W) { return (uint32_t)(PLACE_WINDOW * W * 16 + PLACE_WINDOW * m + PLACE_WINDOW); }
+
+template <int P>
+__device__ __forceinline__ uint32_t max_byte(const uint32_t (&w)[P / 4]) {
+    uint32_t t = w[0];
+#pragma unroll
+    for (int i = 1; i < P / 4; ++i) t = __vmaxu4(t, w[i]);
+    t = __vmaxu4(t, t >> 16);
+    t = __vmaxu4(t, t >> 8);
+    return t & 0xffu;
+}
+
+template <int P>
+__global__ void __launch_bounds__(128) place_rows_kernel(uint4* __restrict__ codes, int64_t n, int64_t n_pad, int m,
+                                                         int W, uint8_t* __restrict__ perm, int first_depth,
+                                                         int last_depth, int steps, uint64_t key) {
+    static_assert(PLACE_WINDOW == 64 && (P == 8 || P == 16), "two positions per lane, phases of 8 or 16 lanes");
+    constexpr int PH = PLACE_WINDOW / P;  // phases per window
+    extern __shared__ __align__(16) unsigned char place_smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
+    const uint32_t per_warp = (place_warp_smem(m, W) + 15u) & ~15u;
+    unsigned char* mine = place_smem + warp * per_warp;
+    uint4* words = reinterpret_cast<uint4*>(mine);                  // [64][W]: the window's rows, in row order
+    const unsigned char* row_codes = mine;                          // row r, sub-space s at r * W * 16 + s
+    unsigned char* cnt = mine + PLACE_WINDOW * W * 16;              // [PH][m][P]
+    unsigned char* order = cnt + PLACE_WINDOW * m;                  // [64]: row at each position
+    const int64_t windows = n_pad / PLACE_WINDOW;
+    for (int64_t win = (int64_t)blockIdx.x * wpb + warp; win < windows; win += (int64_t)gridDim.x * wpb) {
+        const int64_t p0 = win * PLACE_WINDOW;
+        if (p0 + PLACE_WINDOW > n || W > 4) {
+            perm[p0 + lane] = (uint8_t)lane;
+            perm[p0 + 32 + lane] = (uint8_t)(32 + lane);
+            continue;
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int p = h * 32 + lane;
+            const int64_t i = p0 + p;
+            for (int w = 0; w < W; ++w) words[p * W + w] = codes[((i >> 5) * W + w) * 32 + (i & 31)];
+            order[p] = (uint8_t)p;
+        }
+        for (int t = lane; t < PLACE_WINDOW * m; t += 32) cnt[t] = 0;
+        __syncwarp();
+        for (int h = 0; h < 2; ++h) {
+            const int s = lane + 32 * h;
+            if (s < m)
+                for (int p = 0; p < PLACE_WINDOW; ++p)
+                    ++cnt[((p / P) * m + s) * P + (row_codes[p * W * 16 + s] & (P - 1))];
+        }
+        __syncwarp();
+        for (int it = 0; it < steps; ++it) {
+            const uint64_t hsh = mix64(key ^ mix64((uint64_t)win * 0x100000000ull + (uint64_t)it));
+            const int i = (int)(hsh & 63), j = (int)((hsh >> 6) & 63);
+            const int pa = i / P, pb = j / P;
+            if (pa == pb) continue;  // uniform: every lane draws the same pair
+            const int ri = order[i], rj = order[j];
+            int delta = 0;
+            uint32_t na[2][P / 4], nb[2][P / 4];
+            bool moved[2] = {false, false};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int s = lane + 32 * h;
+                if (s >= m) continue;
+                const int ci = row_codes[ri * W * 16 + s] & (P - 1), cj = row_codes[rj * W * 16 + s] & (P - 1);
+                if (ci == cj) continue;
+                const uint32_t* ca = reinterpret_cast<const uint32_t*>(cnt + (pa * m + s) * P);
+                const uint32_t* cb = reinterpret_cast<const uint32_t*>(cnt + (pb * m + s) * P);
+#pragma unroll
+                for (int e = 0; e < P / 4; ++e) {
+                    na[h][e] = ca[e];
+                    nb[h][e] = cb[e];
+                }
+                const int before = (int)max_byte<P>(na[h]) + (int)max_byte<P>(nb[h]);
+                // row ri moves from phase pa to pb, row rj the other way
+                na[h][ci >> 2] -= 1u << (8 * (ci & 3));
+                na[h][cj >> 2] += 1u << (8 * (cj & 3));
+                nb[h][cj >> 2] -= 1u << (8 * (cj & 3));
+                nb[h][ci >> 2] += 1u << (8 * (ci & 3));
+                const int after = (int)max_byte<P>(na[h]) + (int)max_byte<P>(nb[h]);
+                const int wgt = s < first_depth ? 20 : s < last_depth ? 6 : 1;
+                delta += wgt * (after - before);
+                moved[h] = true;
+            }
+            delta = __reduce_add_sync(FULL, delta);
+            if (delta <= 0) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    if (!moved[h]) continue;
+                    const int s = lane + 32 * h;
+                    uint32_t* ca = reinterpret_cast<uint32_t*>(cnt + (pa * m + s) * P);
+                    uint32_t* cb = reinterpret_cast<uint32_t*>(cnt + (pb * m + s) * P);
+#pragma unroll
+                    for (int e = 0; e < P / 4; ++e) {
+                        ca[e] = na[h][e];
+                        cb[e] = nb[h][e];
+                    }
+                }
+                if (lane == 0) {
+                    order[i] = (uint8_t)rj;
+                    order[j] = (uint8_t)ri;
+                }
+            }
+            __syncwarp();
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int p = h * 32 + lane;
+            const int r = order[p];
+            const int64_t i = p0 + p;
+            for (int w = 0; w < W; ++w) codes[((i >> 5) * W + w) * 32 + (i & 31)] = words[r * W + w];
+            perm[i] = (uint8_t)r;
+        }
+        __syncwarp();  // the warp's shared buffers are reused by its next window
     }
 }
 

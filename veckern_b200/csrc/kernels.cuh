@@ -79,6 +79,7 @@ __global__ void __launch_bounds__(256) lut_kernel(const float* __restrict__ cent
 // ------------------------------------------------------------------------------------------------ fused scan
 struct ScanArgs {
     const uint4* codes;  // interleaved layout, n_pad rows
+    const uint8_t* perm; // [n_pad] lane placement: position p holds row (p & ~63) + perm[p]
     const float* lut;    // groups x (Q * m * 256), scan layout
     int2* part;          // [nq][chunks][k] partial lists (dist bits, id)
     int* work_counter;   // dynamic work-item counter, zero before launch
@@ -97,7 +98,7 @@ struct ScanArgs {
 // Shared-memory plan of scan_kernel; host and device compute it with the same function. merge_slots: how many
 // queries' warp lists the item-end merge stages at once (1 or Q).
 struct ScanSmem {
-    uint32_t lut, stage, scratch, queue, ring, bars, flags, total, tile_bytes, lut_bytes;
+    uint32_t lut, stage, scratch, queue, ring, bars, flags, total, tile_bytes, stage_bytes, lut_bytes;
 };
 __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp, int nw, int stages, int k,
                                                    bool prune, int merge_slots) {
@@ -105,9 +106,10 @@ __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp,
     ScanSmem p;
     p.lut_bytes = (uint32_t)Q * m * KSUB * 4u;
     p.tile_bytes = (uint32_t)ilp * W * 512u;
+    p.stage_bytes = p.tile_bytes + (uint32_t)ilp * 32u;  // codes, then the tile's placement bytes
     p.lut = 0;
     p.stage = up(p.lut_bytes, 128);
-    p.scratch = up(p.stage + (uint32_t)nw * stages * p.tile_bytes, 128);
+    p.scratch = up(p.stage + (uint32_t)nw * stages * p.stage_bytes, 128);
     p.queue = up(p.scratch + (uint32_t)merge_slots * nw * k * 8u, 16);
     // the queue holds at most half a tile's (row, query) pairs: with more survivors the tile is finished in full
     p.ring = up(p.queue + (prune ? (uint32_t)nw * 16u * ilp * Q * 8u : 0u), 16);
@@ -123,6 +125,12 @@ __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp,
 // pair per lane costs less than two more Q-wide sub-spaces of every row. Survival curves of partial sums differ
 // between data sets (on the clustered SIFT-shaped mixture at m = 16, 0.15% of the pairs survive 8 sub-spaces; on
 // the Dirichlet-generated codes 72% survive 8, 20% survive 10 and 1.3% survive 12), hence the per-tile choice.
+// Lane placement: within each window of PLACE_WINDOW rows (whole windows below n only), the index stores rows in
+// an order chosen at build time so that the rows one quarter-warp serves in a 16-byte LUT fetch fall into different
+// shared-memory bank groups as often as possible (place_rows_kernel). perm[p] gives the row of position p within
+// its window; ids, and so results, are those of the rows.
+constexpr int PLACE_WINDOW = 64;
+
 __host__ __device__ constexpr int prune_first(int m) { return m <= 16 ? 8 : m <= 32 ? 12 : 24; }
 __host__ __device__ constexpr int prune_last(int m) { return m <= 16 ? 12 : m <= 32 ? 16 : 28; }
 constexpr int PRUNE_DEEPEN = 8;
@@ -216,7 +224,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* my_bars = bars + warp * a.stages;
-    unsigned char* my_stages = smem + plan.stage + (uint32_t)warp * a.stages * plan.tile_bytes;
+    unsigned char* my_stages = smem + plan.stage + (uint32_t)warp * a.stages * plan.stage_bytes;
     int2* my_queue = reinterpret_cast<int2*>(smem + plan.queue) + warp * (16 * ILP * Q);
     int* my_ring = reinterpret_cast<int*>(smem + plan.ring) + warp * a.stages;  // tile held by each slot, -1: none
 
@@ -283,9 +291,10 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
             if (t < ntiles) {
                 my_ring[slot] = t;
                 fence_proxy_async_smem();
-                mbar_arrive_expect_tx(my_bars + slot, plan.tile_bytes);
-                bulk_g2s(my_stages + slot * plan.tile_bytes, a.codes + (t_begin + t) * tile_rows * W,
-                         plan.tile_bytes, my_bars + slot);
+                unsigned char* dst = my_stages + slot * plan.stage_bytes;
+                mbar_arrive_expect_tx(my_bars + slot, plan.stage_bytes);
+                bulk_g2s(dst, a.codes + (t_begin + t) * tile_rows * W, plan.tile_bytes, my_bars + slot);
+                bulk_g2s(dst + plan.tile_bytes, a.perm + (t_begin + t) * tile_rows, (uint32_t)tile_rows, my_bars + slot);
                 ++issued;
             } else {
                 my_ring[slot] = -1;
@@ -311,8 +320,13 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                 break;
             }
             ++consumed;
-            const uint4* st = reinterpret_cast<const uint4*>(my_stages + slot * plan.tile_bytes);
+            const uint4* st = reinterpret_cast<const uint4*>(my_stages + slot * plan.stage_bytes);
+            const uint8_t* st_perm = my_stages + slot * plan.stage_bytes + plan.tile_bytes;
             const int64_t tile_row0 = (t_begin + tile) * tile_rows;
+            // global id of the row at tile position r (lane placement within 64-row windows)
+            auto row_id = [&](int r) {
+                return (int32_t)(a.id_base + ((tile_row0 + r) & ~(int64_t)(PLACE_WINDOW - 1)) + st_perm[r]);
+            };
 
             if constexpr (!PRUNE) {
                 float acc[ILP][Q];
@@ -338,17 +352,17 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                         }
                     }
                 }
-                __syncwarp();  // every lane has consumed the slot (the codes fed the lookups above)
+                int32_t ids[ILP];
+#pragma unroll
+                for (int u = 0; u < ILP; ++u) ids[u] = row_id(u * 32 + lane);
+                __syncwarp();  // every lane has consumed the slot (codes and placement bytes)
                 if (lane == 0) refill();
 
                 bool any = false;
-                int32_t ids[ILP];
                 bool valid[ILP];
 #pragma unroll
                 for (int u = 0; u < ILP; ++u) {
-                    const int64_t row = tile_row0 + u * 32 + lane;
-                    valid[u] = row < a.n;
-                    ids[u] = (int32_t)(a.id_base + row);
+                    valid[u] = tile_row0 + u * 32 + lane < a.n;
 #pragma unroll
                     for (int q = 0; q < Q; ++q) any |= valid[u] && top[q].admits(acc[u][q], ids[u]);
                 }
@@ -420,7 +434,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                     int32_t ids[ILP];
 #pragma unroll
                     for (int u = 0; u < ILP; ++u) {
-                        ids[u] = (int32_t)(a.id_base + tile_row0 + u * 32 + lane);
+                        ids[u] = row_id(u * 32 + lane);
 #pragma unroll
                         for (int q = 0; q < Q; ++q) any |= ((masks[u][q] >> lane) & 1u) && top[q].admits(acc[u][q], ids[u]);
                     }
@@ -479,7 +493,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                                 live = live && !(x > bq);
                             }
                         }
-                        const int32_t id = (int32_t)(a.id_base + tile_row0 + r);
+                        const int32_t id = row_id(r);
                         if (__any_sync(FULL, live)) {  // usually every pair of the batch was abandoned
 #pragma unroll
                             for (int qq = 0; qq < Q; ++qq) {
@@ -523,7 +537,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
         if (*s_abort) continue;  // uniform: the next (A) exits the loop
         // Merge the NW warp lists of each query into the item's partial list: merge_slots queries at a time,
         // query q0 + j merged by warp j.
-        auto merge_and_publish = [&](int64_t qi, const int2* slot_lists) {
+        auto merge_and_publish = [&](int64_t qi, const int2* slot_lists, float kb) {
             WarpTopK<S> mt;
             mt.init();
             const int total = NW * a.k;
@@ -537,9 +551,12 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                 // Fold the item's list into the query's global list of the best pairs seen so far, whose k-th
                 // distance bounds the query for every other warp. Chunks cover disjoint rows, so the union has
                 // no duplicates. If another block holds the lock the fold is skipped: only the bound gets
-                // weaker, never wrong.
+                // weaker, never wrong. kb is an upper bound of the query's bound (this warp's last view): when
+                // the item's best pair is not below it, the fold cannot lower the bound (fewer than k pairs of
+                // the union lie below it) and is skipped, which late in a scan is nearly every item.
+                const bool useful = __shfl_sync(FULL, mt.d[0], 0) < kb;
                 int got = 0;
-                if (lane == 0) got = atomicCAS(a.glock + qi, 0, 1) == 0;
+                if (lane == 0 && useful) got = atomicCAS(a.glock + qi, 0, 1) == 0;
                 if (__shfl_sync(FULL, got, 0)) {
                     __threadfence();
                     int2* gl = a.glist + qi * a.k;
@@ -553,7 +570,8 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                     __syncwarp();
                     if (lane == 0) atomicExch(a.glock + qi, 0);
                 }
-                if (lane == 0 && mt.thr_i != SENTINEL_ID) atomicMin(a.bound + qi, __float_as_uint(mt.thr_d));
+                if (lane == 0 && mt.thr_i != SENTINEL_ID && mt.thr_d < kb)
+                    atomicMin(a.bound + qi, __float_as_uint(mt.thr_d));
             }
         };
         if (a.merge_slots >= Q) {
@@ -561,7 +579,13 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
             for (int q = 0; q < Q; ++q) top[q].store(scratch + (q * NW + warp) * a.k, a.k);
             __syncthreads();
             const int64_t qi = (int64_t)g * Q + warp;
-            if (warp < Q && qi < a.nq) merge_and_publish(qi, scratch + warp * NW * a.k);
+            float kb = __int_as_float(0x7f800000);
+            if constexpr (PRUNE) {
+#pragma unroll
+                for (int q = 0; q < Q; ++q)
+                    if (warp == q) kb = known[q];
+            }
+            if (warp < Q && qi < a.nq) merge_and_publish(qi, scratch + warp * NW * a.k, kb);
             __syncthreads();
         } else {
 #pragma unroll
@@ -570,7 +594,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                 if (qi < a.nq) {  // uniform
                     top[q].store(scratch + warp * a.k, a.k);
                     __syncthreads();
-                    if (warp == 0) merge_and_publish(qi, scratch);
+                    if (warp == 0) merge_and_publish(qi, scratch, PRUNE ? known[q] : __int_as_float(0x7f800000));
                     __syncthreads();
                 }
             }

@@ -144,6 +144,7 @@ struct vk_index {
     int64_t n = 0, n_pad = 0, id_base = 0;
     float* centroids = nullptr;
     uint4* codes = nullptr;
+    uint8_t* perm = nullptr;  // [n_pad] lane placement (place_rows_kernel)
     cudaStream_t stream = nullptr;
     DevBuf<float> queries, lut, dists;
     DevBuf<int2> part, out;
@@ -162,6 +163,7 @@ struct vk_index {
         if (stream) cudaStreamDestroy(stream);
         if (centroids) cudaFree(centroids);
         if (codes) cudaFree(codes);
+        if (perm) cudaFree(perm);
         if (flags) cudaFree(flags);
     }
 };
@@ -311,6 +313,7 @@ int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk
         VK_TRY_CUDA(cudaMemsetAsync(ix->flags, 0, sizeof(int), st));
         vk::ScanArgs a{};
         a.codes = ix->codes;
+        a.perm = ix->perm;
         a.lut = ix->lut.ptr;
         a.part = ix->part.ptr;
         a.work_counter = ix->flags;
@@ -409,7 +412,28 @@ int create_common(int device, const float* centroids, int m, int dsub, int64_t n
     VK_TRY_CUDA(cudaMemcpyAsync(ix->centroids, centroids, cbytes, cudaMemcpyHostToDevice, ix->stream));
     VK_TRY_CUDA(cudaMalloc(&ix->codes, (size_t)ix->n_pad * ix->W * sizeof(uint4)));
     VK_TRY_CUDA(cudaMemsetAsync(ix->codes, 0, (size_t)ix->n_pad * ix->W * sizeof(uint4), ix->stream));
+    VK_TRY_CUDA(cudaMalloc(&ix->perm, (size_t)ix->n_pad));
     return VK_OK;
+}
+
+// Lane placement of the rows of every 64-row window (vk::place_rows_kernel), on the index stream after the codes
+// are in place. The objective follows the LUT layout the default plan picks for this m: 16-byte entries (Q >= 4)
+// up to m = 32, 8-byte entries (Q = 2) beyond; its weights follow the pruned scan's phase-A depths.
+cudaError_t place_rows(vk_index* ix) {
+    constexpr int kSteps = 4096;
+    constexpr uint64_t kKey = 0x6c616e6570696b73ull;
+    const int mt = (ix->m == 16 || ix->m == 32 || ix->m == 64) ? ix->m : 0;
+    const int first = mt ? vk::prune_first(mt) : 0, last = mt ? vk::prune_last(mt) : 0;
+    const uint32_t smem = ix->W > 4 ? 0u : 4 * ((vk::place_warp_smem(ix->m, ix->W) + 15u) & ~15u);  // <= 33 KB
+    const int64_t windows = ix->n_pad / vk::PLACE_WINDOW;
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(windows, 4), (int64_t)ix->sm_count * 16));
+    if (ix->m <= 32)
+        vk::place_rows_kernel<8><<<grid, 128, smem, ix->stream>>>(ix->codes, ix->n, ix->n_pad, ix->m, ix->W, ix->perm,
+                                                                   first, last, kSteps, kKey);
+    else
+        vk::place_rows_kernel<16><<<grid, 128, smem, ix->stream>>>(ix->codes, ix->n, ix->n_pad, ix->m, ix->W,
+                                                                    ix->perm, first, last, kSteps, kKey);
+    return cudaGetLastError();
 }
 
 unsigned grid_for(int64_t total, int sm_count) {
@@ -485,6 +509,7 @@ int vk_index_create(int device, const float* centroids, int m, int dsub, const u
             if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);  // staging is reused
         }
         if (staging) cudaFree(staging);
+        if (e == cudaSuccess) e = place_rows(ix);
         if (e != cudaSuccess) rc = fail(VK_ERR_CUDA, "code upload failed: %s", cudaGetErrorString(e));
     }
     if (rc == VK_OK) {
@@ -510,6 +535,7 @@ int vk_index_create_from_device(int device, const float* centroids, int m, int d
         vk::interleave_kernel<<<grid_for(ix->n_pad * ix->W, ix->sm_count), 256, 0, ix->stream>>>(d_codes, 0, n, n, m,
                                                                                                    ix->W, ix->codes);
         cudaError_t e = cudaGetLastError();
+        if (e == cudaSuccess) e = place_rows(ix);
         if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);
         if (e != cudaSuccess) rc = fail(VK_ERR_CUDA, "index build failed: %s", cudaGetErrorString(e));
     }
@@ -540,6 +566,7 @@ int vk_index_create_generated(int device, const float* centroids, int m, int dsu
                 vk::mix64(seed), d_cdf, clusters, m, ix->W, row_first, n, ix->n_pad, ix->codes);
             e = cudaGetLastError();
         }
+        if (e == cudaSuccess) e = place_rows(ix);
         if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);
         if (d_cdf) cudaFree(d_cdf);
         if (e != cudaSuccess) rc = fail(VK_ERR_CUDA, "code generation failed: %s", cudaGetErrorString(e));
@@ -574,8 +601,8 @@ int vk_index_get_codes(const vk_index_t* ix, int64_t first, int64_t count, uint8
     DeviceGuard guard(ix->device);
     uint8_t* d = nullptr;
     VK_TRY_CUDA(cudaMalloc(&d, (size_t)count * ix->m));
-    vk::deinterleave_kernel<<<grid_for(count * ix->m, ix->sm_count), 256, 0, ix->stream>>>(ix->codes, first, count,
-                                                                                           ix->m, ix->W, d);
+    vk::deinterleave_kernel<<<grid_for((count + 2 * vk::PLACE_WINDOW) * ix->m, ix->sm_count), 256, 0, ix->stream>>>(
+        ix->codes, ix->perm, first, count, ix->m, ix->W, d);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaMemcpyAsync(out, d, (size_t)count * ix->m, cudaMemcpyDeviceToHost, ix->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);
@@ -699,8 +726,8 @@ int vk_distances(vk_index_t* ix, const float* queries, int64_t nq, int variant, 
         const int threads = t.scan_threads;
         const int64_t bx = std::max<int64_t>(1, std::min<int64_t>(ceil_div(ix->n, threads),
                                                                   ceil_div(8LL * ix->sm_count, b)));
-        vk::dist_kernel<<<dim3((unsigned)bx, (unsigned)b), threads, lut_smem, st>>>(ix->codes, ix->lut.ptr, ix->n,
-                                                                                    ix->m, ix->W, ix->dists.ptr);
+        vk::dist_kernel<<<dim3((unsigned)bx, (unsigned)b), threads, lut_smem, st>>>(ix->codes, ix->perm, ix->lut.ptr,
+                                                                                    ix->n, ix->m, ix->W, ix->dists.ptr);
         VK_TRY_CUDA(cudaGetLastError());
         VK_TRY_CUDA(cudaEventRecord(ev[3], st));
         VK_TRY_CUDA(cudaMemcpyAsync(out + q0 * ix->n, ix->dists.ptr, (size_t)b * ix->n * sizeof(float),
@@ -910,6 +937,7 @@ extern "C" int vk_search_noalloc(vk_index_t* ix, const float* d_queries, int64_t
     {
         vk::ScanArgs a{};
         a.codes = ix->codes;
+        a.perm = ix->perm;
         a.lut = lut;
         a.part = part;
         a.work_counter = flags;
