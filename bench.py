@@ -158,6 +158,17 @@ class ClockSampler:
                 "power_w_max": round(max(r[2] for r in rows), 1)}
 
 
+# DRAM bytes per launch of the default scan kernel from the ncu capture summarised in profiles/ (same bench command,
+# one GPU); reported only for the workload it was captured on.
+NCU_TRAFFIC = {("c1", 1_000_000, 16, 1000, 10): {"dram_bytes_per_launch": 33_596_672,
+                                                 "source": "profiles/scan_kernel_c1_m16.md (ncu, dram__bytes_read.sum "
+                                                           "+ dram__bytes_write.sum)"}}
+
+
+def ncu_traffic(config, spec, world):
+    return NCU_TRAFFIC.get((config, spec["n"], spec["m"], spec["nq"], spec["k"])) if world == 1 else None
+
+
 def lookup_wavefront_model(codes: np.ndarray, Q: int, sample_rows: int = 1 << 17) -> float:
     """Mean shared-memory wavefronts per warp-wide LUT fetch for these codes under the scan kernel's layout
     ([s][c][Q] entries: LDS.32 / .64 / .128 for Q = 1 / 2 / 4 and 8; 32 consecutive rows per warp instruction):
@@ -408,8 +419,14 @@ def run_ours(args):
         achieved = lookups / (scan_mean / 1e3)
         smem_peak_bytes = 128.0 * info.sm_count * sm_mhz * 1e6
         Q = s.last_launch().queries_per_block
-        codes_for_model = w.codes if w.codes is not None else None
-        wf = lookup_wavefront_model(codes_for_model, Q) if codes_for_model is not None else None
+        wf = wf_rows = None
+        if w.codes is not None:
+            # the device layout: rows of whole 64-row windows in the index's lane placement
+            perm = s.get_placement()
+            full = w.codes.shape[0] // 64 * 64
+            placed = np.concatenate([w.codes[(np.arange(full) & ~63) + perm[:full]], w.codes[full:]])
+            wf = lookup_wavefront_model(placed, Q)
+            wf_rows = lookup_wavefront_model(w.codes, Q)
         per_fetch = 4 if Q >= 4 else Q  # lookups served per warp LUT fetch per lane
         fetches = lookups / 32.0 / per_fetch
         floor_ms = fetches * wf / (info.sm_count * sm_mhz * 1e6) * 1e3 if wf else None
@@ -417,13 +434,15 @@ def run_ours(args):
             "bound": "smem",
             "achieved": round(achieved * 4 / 1e9, 1), "peak": round(smem_peak_bytes / 1e9, 1), "unit": "GB/s",
             "frac": round(achieved * 4 / smem_peak_bytes, 4),
-            "traffic": None,
+            "traffic": ncu_traffic(args.config, spec, world),
             "note": ("achieved = algorithmic LUT bytes (4 B per (query, row, sub-space) lookup, nq*n*m per launch) / "
                      "scan-kernel event time; peak = shared-memory bandwidth 128 B/clk/SM x SMs x median SM clock "
                      "sampled under load. lookup_floor: time the full scan's conflict-inclusive LDS wavefronts need "
-                     "(bank-conflict model of these codes, one wavefront per clock per SM); the default kernel "
+                     "(bank-conflict model of these codes in the index's lane placement, one wavefront per clock "
+                     "per SM; wavefronts_per_fetch_row_order: the same codes in row order); the default kernel "
                      "abandons most pairs early, so it can beat that floor"),
             "lookup_floor": {"wavefronts_per_fetch": round(wf, 3) if wf else None,
+                             "wavefronts_per_fetch_row_order": round(wf_rows, 3) if wf_rows else None,
                              "floor_ms": round(floor_ms, 4) if floor_ms else None,
                              "kernel_ms": round(scan_mean, 4),
                              "frac": round(floor_ms / scan_mean, 4) if floor_ms else None,

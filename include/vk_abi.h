@@ -128,6 +128,12 @@ int vk_index_info(const vk_index_t* index, int64_t* n, int* m, int* dsub, int64_
 /* Copies the index's row-major codes for rows [first, first + count) back to host memory (tests, tools). */
 int vk_index_get_codes(const vk_index_t* index, int64_t first, int64_t count, uint8_t* out);
 
+/* Lane placement of the device layout (no counterpart in the reference): out[j] = the row, relative to its window
+ * of 64 positions, stored at position first + j, for j < count. The index stores the rows of every whole 64-row
+ * window in an order chosen at build time to cut shared-memory bank conflicts of the LUT lookups; ids and results
+ * are unaffected. first must be a multiple of 64 and first + count <= n rounded up to 128 (diagnostics, tests). */
+int vk_index_get_placement(const vk_index_t* index, int64_t first, int64_t count, uint8_t* out);
+
 /* Replaces PQSearcher::search (src/cuda/searcher.cu:466-520): HOST queries (nq x d fp32) in, HOST results
  * (nq x k vk_neighbor_t, ascending) out, 1 <= k <= min(128, n). Synchronous. timings/shape may be NULL.
  * `variant` only selects the reference's validation rules (m % 16 == 0 for variants 2, 6, 7, 8). */

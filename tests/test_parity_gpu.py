@@ -308,6 +308,44 @@ def test_index_codes_roundtrip(golden):
         assert np.array_equal(s.get_codes(20_000, 11), g["codes"][20_000:])
 
 
+def quarter_warp_wavefronts(codes, lanes=8):
+    """Mean shared-memory wavefronts of one 16-byte LUT fetch per 32 positions (phases of `lanes` lanes, entry c of a
+    table in bank group c % lanes; equal codes in a phase are one access)."""
+    n, m = codes.shape
+    c = codes[: n // 32 * 32].reshape(-1, 32 // lanes, lanes, m).astype(np.int64)
+    total = 0
+    for g in c.reshape(-1, lanes, m):
+        for s in range(m):
+            u = np.unique(g[:, s])
+            total += np.bincount(u % lanes, minlength=lanes).max()
+    return total / (len(c) * m)
+
+
+@pytest.mark.parametrize("m,dsub", [(16, 8), (32, 4), (64, 2), (20, 4)])
+def test_lane_placement(m, dsub):
+    """Rows of every whole 64-row window are permuted (ids unaffected), partial windows keep the identity, codes
+    read back in row order, and the placement lowers the bank-group load of 16-byte LUT fetches."""
+    rng = np.random.default_rng(m)
+    n = 50_003
+    cent = rng.normal(size=(m, 256, dsub)).astype(np.float32)
+    codes = (rng.normal(128, 40, size=(n, m)).clip(0, 255)).astype(np.uint8)  # skewed, like trained codes
+    with PQSearcher(cent, codes) as s:
+        perm = s.get_placement()
+        assert np.array_equal(s.get_codes(), codes)
+        assert np.array_equal(s.get_codes(12_345, 777), codes[12_345:12_345 + 777])
+    full = n // 64 * 64
+    windows = perm[:full].reshape(-1, 64)
+    assert (np.sort(windows, axis=1) == np.arange(64)).all()
+    assert (windows != np.arange(64)).any(axis=1).mean() > 0.9
+    assert np.array_equal(perm[full:], np.tile(np.arange(64, dtype=np.uint8), (len(perm) - full) // 64))
+    placed = codes[(np.arange(full) & ~63) + perm[:full]]
+    if m <= 32:  # 16-byte entries; the placement weighs the pruned scan's phase-A sub-spaces most
+        ss = {16: 8, 32: 12}.get(m, m)
+        before = quarter_warp_wavefronts(codes[:8192, :ss])
+        after = quarter_warp_wavefronts(placed[:8192, :ss])
+        assert after < 0.9 * before, (before, after)
+
+
 def test_rerank_kernel_matches_reference(golden, port):
     """GPU exact re-rank == the reference's rerank_exact (fixture) and the oracle (duplicates, padding, ties)."""
     import torch

@@ -69,6 +69,7 @@ ABI = {
     "vk_index_info": (C.c_int, [_vp, C.POINTER(_i64), C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(_i64),
                                 C.POINTER(C.c_int)]),
     "vk_index_get_codes": (C.c_int, [_vp, _i64, _i64, _vp]),
+    "vk_index_get_placement": (C.c_int, [_vp, _i64, _i64, _vp]),
     "vk_search": (C.c_int, [_vp, _vp, _i64, C.c_int, C.c_int, C.POINTER(Tuning), _vp, C.POINTER(Timings),
                             C.POINTER(LaunchShape)]),
     "vk_search_device": (C.c_int, [_vp, _vp, _i64, C.c_int, C.POINTER(Tuning), _vp, _vp]),

@@ -611,6 +611,17 @@ int vk_index_get_codes(const vk_index_t* ix, int64_t first, int64_t count, uint8
     return VK_OK;
 }
 
+int vk_index_get_placement(const vk_index_t* ix, int64_t first, int64_t count, uint8_t* out) {
+    if (!ix || (!out && count > 0)) return fail(VK_ERR_INVALID, "index and out must not be NULL");
+    if (first < 0 || count < 0 || first % vk::PLACE_WINDOW != 0 || first + count > ix->n_pad)
+        return fail(VK_ERR_INVALID, "position range out of bounds");
+    if (count == 0) return VK_OK;
+    DeviceGuard guard(ix->device);
+    VK_TRY_CUDA(cudaMemcpyAsync(out, ix->perm + first, (size_t)count, cudaMemcpyDeviceToHost, ix->stream));
+    VK_TRY_CUDA(cudaStreamSynchronize(ix->stream));
+    return VK_OK;
+}
+
 int vk_search(vk_index_t* ix, const float* queries, int64_t nq, int k, int variant, const vk_tuning_t* tuning,
               vk_neighbor_t* out, vk_timings_t* timings, vk_launch_shape_t* shape) {
     if (!ix) return fail(VK_ERR_INVALID, "index must not be NULL");

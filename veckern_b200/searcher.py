@@ -221,6 +221,13 @@ class PQSearcher:
         check(lib().vk_index_get_codes(self._h, first, count, ptr(out)), "get_codes")
         return out
 
+    def get_placement(self) -> np.ndarray:
+        """[n_pad] uint8: row (within its 64-position window) stored at each position of the device layout."""
+        n_pad = (self.n + 127) // 128 * 128
+        out = np.empty(n_pad, np.uint8)
+        check(lib().vk_index_get_placement(self._h, 0, n_pad, ptr(out)), "get_placement")
+        return out
+
 
 def _stream_handle(stream):
     """cudaStream_t of a torch.cuda.Stream / raw handle; None -> torch's current stream (0 = default stream)."""
