@@ -393,7 +393,9 @@ def run_ours(args):
         if rank == 0:
             from veckern_b200 import configs
             full = configs.make(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k, encode=gpu_encoder())
-            with PQSearcher(full.centroids, full.codes, device=local) as one:
+            one = (PQSearcher(full.centroids, full.codes, device=local) if full.codes is not None else
+                   PQSearcher.generated(full.centroids, spec["code_seed"], full.cdf, 0, n, device=local))
+            with one:
                 one.set_tuning(tuning)
                 ref = torch.empty((nq, k), dtype=torch.int64, device="cuda")
                 one.search_device(d_q, k, ref, stream)
