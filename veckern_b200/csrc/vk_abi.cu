@@ -227,21 +227,30 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     const int64_t tile_rows = 32 * p.ilp;
     const int64_t tiles = ix->n_pad / tile_rows;
     const int64_t max_chunks = std::max<int64_t>(1, tiles / (2 * nw));  // >= 2 tiles per warp per chunk
-    // The pruned scan tightens each query's bound as chunks complete: use enough chunks for that to pay off
-    // (up to 48), but keep chunks of at least 16K rows so that each item's LUT load stays amortised.
-    const int64_t prune_chunks = p.prune ? std::max<int64_t>(1, std::min<int64_t>(48, ix->n_pad / 16384)) : 1;
-    const int64_t min_chunks =
-        std::min(max_chunks, std::max<int64_t>(ceil_div(ix->n_pad, kMaxRowsPerChunk), prune_chunks));
-    int64_t chunks = min_chunks;
+    // Chunk count: a wave model over the resident blocks, time ~ ceil(items / resident) * (rows per chunk + a
+    // per-item overhead in rows of scan work), minimised over a range of chunk counts. The pruned scan tightens each
+    // query's bound whenever one of its chunks completes, so its chunks stay between 16K and 64K rows (up to 48
+    // chunks; more only when the L2 locality cap asks for it), and its per-item overhead is higher (list merge and
+    // fold at every item end: about 2K rows of work, measured).
+    const int64_t l2_chunks = ceil_div(ix->n_pad, kMaxRowsPerChunk);
+    int64_t lo = l2_chunks, hi = l2_chunks + 8 * resident;
+    double item_rows = 512.0;
+    if (p.prune) {
+        lo = std::max(l2_chunks, std::min<int64_t>(48, ceil_div(ix->n_pad, 65536)));
+        hi = std::max(lo, std::min<int64_t>(48, ix->n_pad / 16384));
+        hi = std::max(hi, ceil_div(resident, p.groups));  // few query groups: spread their rows over every SM
+        item_rows = 2048.0;
+    }
+    lo = std::min(lo, max_chunks);
+    hi = std::min(hi, max_chunks);
+    int64_t chunks = lo;
     if (t.blocks_per_query > 0) {
         chunks = std::min<int64_t>(t.blocks_per_query, max_chunks);
     } else {
-        const double lut_rows = 512.0;  // LUT reload per item, in rows of scan work
         double best = 1e300;
-        const int64_t hi = std::min(max_chunks, min_chunks + 8 * resident);
-        for (int64_t c = min_chunks; c <= hi; ++c) {
+        for (int64_t c = lo; c <= hi; ++c) {
             const double waves = (double)ceil_div((int64_t)p.groups * c, resident);
-            const double cost = waves * ((double)ix->n_pad / c + lut_rows);
+            const double cost = waves * ((double)ix->n_pad / c + item_rows);
             if (cost < best * 0.999) {
                 best = cost;
                 chunks = c;
