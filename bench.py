@@ -205,13 +205,18 @@ def build_workload(args, rank: int, world: int):
     spec = configs.spec(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k)
     sh = shard_of(spec["n"], world, rank)
     w = configs.make(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k, encode=gpu_encoder(),
-                     rows=(sh.lo, sh.hi))
+                     train=gpu_trainer(), rows=(sh.lo, sh.hi))
     return spec, w, sh
 
 
 def gpu_encoder():
     from veckern_b200.data import gpu_encoder as enc
     return enc()
+
+
+def gpu_trainer():
+    from veckern_b200.data import gpu_trainer as tr
+    return tr()
 
 
 # ------------------------------------------------------------------------------------------------ reference arm
@@ -392,7 +397,8 @@ def run_ours(args):
         torch.cuda.synchronize()
         if rank == 0:
             from veckern_b200 import configs
-            full = configs.make(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k, encode=gpu_encoder())
+            full = configs.make(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k, encode=gpu_encoder(),
+                                train=gpu_trainer())
             one = (PQSearcher(full.centroids, full.codes, device=local) if full.codes is not None else
                    PQSearcher.generated(full.centroids, spec["code_seed"], full.cdf, 0, n, device=local))
             with one:

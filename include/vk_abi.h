@@ -177,6 +177,13 @@ int vk_rerank_device(int device, const float* d_base, int64_t n, int d, const fl
 int vk_encode_device(int device, const float* centroids, int m, int dsub, const float* d_x, int64_t n,
                      uint8_t* d_codes, void* stream);
 
+/* Replaces ProductQuantizer::train (src/cpu/pq.cpp:31-69) for a training set in DEVICE memory (n x d fp32,
+ * n >= 256, d = m * dsub, dsub <= 128): the same std::mt19937_64 draws (one shuffle per sub-space, rng() % n per
+ * empty cluster) and the same arithmetic (l2sq assignment, first minimum wins; sums in row order; sum / count),
+ * so the HOST output `centroids` ([m][256][dsub] fp32) is bit-identical to the reference's. Synchronous. */
+int vk_pq_train_device(int device, const float* d_x, int64_t n, int d, int m, int64_t iters, uint64_t seed,
+                       float* centroids, void* stream);
+
 /* Generates rows [row_first, row_first + n) of the synthetic code generator into DEVICE memory (row-major n x m);
  * the same integers as vk_gen_codes_host. */
 int vk_gen_codes_device(int device, uint64_t seed, const uint32_t* cdf, int clusters, int m, int64_t row_first,

@@ -346,6 +346,29 @@ def test_lane_placement(m, dsub):
         assert after < 0.9 * before, (before, after)
 
 
+@pytest.mark.parametrize("m,iters", [(16, 5), (32, 3), (64, 2), (4, 2), (1, 1), (16, 0)])
+def test_pq_train_device_matches_host(m, iters):
+    """vk_pq_train_device == ProductQuantizer::train's steps on the host (itself pinned to the reference by
+    test_host.py): same draws, same arithmetic, bit-identical centroids."""
+    from veckern_b200 import data
+    x = data.gen_mixture(0, 0, 12_000, 128)
+    host = data.pq_train(x, m, iters, 7)
+    dev = data.pq_train_gpu(x, m, iters, 7)
+    assert np.array_equal(bits(host), bits(dev))
+
+
+def test_pq_train_device_reseeds_empty_clusters():
+    """Few distinct points: duplicate initial centroids leave clusters empty, which are re-seeded with rng() % n
+    draws in cluster order (pq.cpp:60-63)."""
+    from veckern_b200 import data
+    rng = np.random.default_rng(3)
+    pts = rng.normal(size=(40, 32)).astype(np.float32)
+    x = pts[rng.integers(0, 40, size=700)]
+    host = data.pq_train(x, 4, 4, 11)
+    dev = data.pq_train_gpu(x, 4, 4, 11)
+    assert np.array_equal(bits(host), bits(dev))
+
+
 def test_rerank_kernel_matches_reference(golden, port):
     """GPU exact re-rank == the reference's rerank_exact (fixture) and the oracle (duplicates, padding, ties)."""
     import torch

@@ -79,6 +79,7 @@ ABI = {
     "vk_merge_topk_device": (C.c_int, [C.c_int, _vp, _i64, C.c_int, C.c_int, _i64, _i64, C.c_int, _vp, _vp]),
     "vk_rerank_device": (C.c_int, [C.c_int, _vp, _i64, C.c_int, _vp, _i64, _vp, C.c_int, C.c_int, _vp, _vp]),
     "vk_encode_device": (C.c_int, [C.c_int, _vp, C.c_int, C.c_int, _vp, _i64, _vp, _vp]),
+    "vk_pq_train_device": (C.c_int, [C.c_int, _vp, _i64, C.c_int, C.c_int, _i64, _u64, _vp, _vp]),
     "vk_gen_codes_device": (C.c_int, [C.c_int, _u64, _vp, C.c_int, C.c_int, _i64, _i64, _vp, _vp]),
     "vk_search_noalloc": (C.c_int, [_vp, _vp, _i64, C.c_int, C.POINTER(Tuning), _vp, _vp]),
 }

@@ -63,11 +63,13 @@ def spec(name: str, **overrides) -> dict:
 
 
 def make(name: str, *, n: int | None = None, m: int | None = None, nq: int | None = None, k: int | None = None,
-         keep_base: bool = False, encode=None, rows: tuple[int, int] | None = None) -> Workload:
-    """Generates config `name` (optionally resized). encode(centroids, x) -> codes may be given to encode on the
-    GPU; the default encodes on the host. rows=(lo, hi): only that shard of the database is generated and encoded
-    (codes[i] is row lo + i); the codebooks are the same as for the whole database."""
+         keep_base: bool = False, encode=None, train=None, rows: tuple[int, int] | None = None) -> Workload:
+    """Generates config `name` (optionally resized). encode(centroids, x) -> codes and train(x, m, iters, seed) ->
+    centroids may be given to run on the GPU (same results); the defaults run on the host. rows=(lo, hi): only that
+    shard of the database is generated and encoded (codes[i] is row lo + i); the codebooks are the same as for the
+    whole database."""
     s = spec(name, n=n, m=m, nq=nq, k=k)
+    train_fn = train
     d = s["d"]
     lo, hi = rows if rows is not None else (0, s["n"])
     if s["kind"] == "generated":
@@ -78,13 +80,13 @@ def make(name: str, *, n: int | None = None, m: int | None = None, nq: int | Non
     if s["kind"] == "normal":
         x = data.gen_normal(s["data_seed"], s["n"], d)  # training draws from all rows
         q = data.gen_normal(s["query_seed"], s["nq"], d)
-        train = x
+        train_x = x
         x = x[lo:hi]
     else:
         q = data.gen_mixture(s["mix_seed"], s["query_seed"], s["nq"], d)
         t = min(s["train_rows"], s["n"])
-        train = data.gen_mixture(s["mix_seed"], s["mix_seed"], t, d)  # rows [0, t): the database's first rows
-        cent = data.pq_train(train, s["m"], s["pq_iters"], s["pq_seed"])
+        train_x = data.gen_mixture(s["mix_seed"], s["mix_seed"], t, d)  # rows [0, t): the database's first rows
+        cent = (train_fn or data.pq_train)(train_x, s["m"], s["pq_iters"], s["pq_seed"])
         enc = encode or data.pq_encode
         if keep_base or hi - lo <= SLICE_ROWS:
             x = data.gen_mixture(s["mix_seed"], s["mix_seed"], hi - lo, d, row0=lo)
@@ -98,7 +100,7 @@ def make(name: str, *, n: int | None = None, m: int | None = None, nq: int | Non
         w = Workload(name, s, cent, q, codes=codes, base=x if keep_base else None)
         w.extra["row0"] = lo
         return w
-    cent = data.pq_train(train, s["m"], s["pq_iters"], s["pq_seed"])
+    cent = (train_fn or data.pq_train)(train_x, s["m"], s["pq_iters"], s["pq_seed"])
     codes = (encode or data.pq_encode)(cent, x)
     w = Workload(name, s, cent, q, codes=codes, base=x if keep_base else None)
     w.extra["row0"] = lo

@@ -228,6 +228,87 @@ __global__ void gen_rows_kernel(uint64_t key, const uint32_t* __restrict__ cdf, 
     }
 }
 
+// ------------------------------------------------------------------------------------------------ PQ training
+// Lloyd iterations of ProductQuantizer::train (src/cpu/pq.cpp:31-69) for one sub-space s, bit-identical to it:
+// the assignment is the encoder's nearest centroid (strict <, first minimum wins, from FLT_MAX; pq.cpp:11-22) and
+// each centroid's sums are accumulated in row order from +0 (pq.cpp:55-58), then divided by the count as a float
+// (pq.cpp:64). The host drives the loop and the std::mt19937_64 draws (shuffle, empty-cluster reseeds).
+
+// cent[c] = sub-vector s of row rows[c], c < 256 (the initial centroids: the first 256 rows of the shuffle).
+__global__ void train_gather_kernel(const float* __restrict__ x, int d, int s, int dsub,
+                                    const int64_t* __restrict__ rows, float* __restrict__ cent) {
+    for (int t = threadIdx.x; t < KSUB * dsub; t += blockDim.x) {
+        const int c = t / dsub, j = t - c * dsub;
+        cent[t] = x[rows[c] * d + (int64_t)s * dsub + j];
+    }
+}
+
+// assign[i] = nearest centroid of row i's sub-vector s; the 256 centroids in shared memory.
+__global__ void __launch_bounds__(256) train_assign_kernel(const float* __restrict__ x, int64_t n, int d, int s,
+                                                           int dsub, const float* __restrict__ cent,
+                                                           int* __restrict__ assign) {
+    extern __shared__ float tcen[];  // [256][dsub]
+    for (int t = threadIdx.x; t < KSUB * dsub; t += blockDim.x) tcen[t] = cent[t];
+    __syncthreads();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float* v = x + i * d + (int64_t)s * dsub;
+        int best = 0;
+        float best_dist = FLT_MAX;
+        for (int c = 0; c < KSUB; ++c) {
+            float acc = 0.f;
+            for (int j = 0; j < dsub; ++j) {
+                const float diff = __fsub_rn(v[j], tcen[c * dsub + j]);
+                acc = __fadd_rn(acc, __fmul_rn(diff, diff));
+            }
+            if (acc < best_dist) {
+                best_dist = acc;
+                best = c;
+            }
+        }
+        assign[i] = best;
+    }
+}
+
+// One warp per centroid c: sums[c] = sub-vectors of the rows assigned to c, added in row order; counts[c].
+// Lane l holds components l, l + 32, ... (dsub <= 128).
+__global__ void __launch_bounds__(256) train_sums_kernel(const float* __restrict__ x, int64_t n, int d, int s, int dsub,
+                                                         const int* __restrict__ assign, float* __restrict__ sums,
+                                                         int* __restrict__ counts) {
+    const int lane = threadIdx.x & 31;
+    const int c = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (c >= KSUB) return;  // warp-uniform
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    int count = 0;
+    for (int64_t i0 = 0; i0 < n; i0 += 32) {
+        const int64_t i = i0 + lane;
+        unsigned mask = __ballot_sync(FULL, i < n && assign[i] == c);
+        count += __popc(mask);
+        while (mask) {
+            const int64_t row = i0 + __ffs(mask) - 1;
+            mask &= mask - 1;
+            const float* v = x + row * d + (int64_t)s * dsub;
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+                if (lane + 32 * r < dsub) acc[r] = __fadd_rn(acc[r], v[lane + 32 * r]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+        if (lane + 32 * r < dsub) sums[c * dsub + lane + 32 * r] = acc[r];
+    if (lane == 0) counts[c] = count;
+}
+
+// cent[c] = sums[c] / counts[c], or sub-vector s of row reseed[c] for an empty cluster (pq.cpp:60-66).
+__global__ void train_update_kernel(const float* __restrict__ x, int d, int s, int dsub, const float* __restrict__ sums,
+                                    const int* __restrict__ counts, const int64_t* __restrict__ reseed,
+                                    float* __restrict__ cent) {
+    for (int t = threadIdx.x; t < KSUB * dsub; t += blockDim.x) {
+        const int c = t / dsub, j = t - c * dsub;
+        cent[t] = counts[c] == 0 ? x[reseed[c] * d + (int64_t)s * dsub + j]
+                                 : __fdiv_rn(sums[t], (float)counts[c]);
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ encode
 // Nearest centroid per (row, sub-space) under the reference's l2sq, strict < so the first minimum wins
 // (src/cpu/pq.cpp:11-22, 71-76). grid (ceil(n / 256), m), block 256; sub-space centroids in shared memory.

@@ -14,6 +14,9 @@
 #include <cstring>
 #include <limits>
 #include <mutex>
+#include <numeric>
+#include <random>
+#include <vector>
 #include <string>
 
 #include "../../include/vk_abi.h"
@@ -842,6 +845,64 @@ int vk_encode_device(int device, const float* centroids, int m, int dsub, const 
     vk::encode_kernel<<<dim3((unsigned)ceil_div(n, 256), m), 256, smem, st>>>(d_cen, m, dsub, d_x, n, d_codes);
     VK_TRY_CUDA(cudaGetLastError());
     VK_TRY_CUDA(cudaFreeAsync(d_cen, st));
+    return VK_OK;
+}
+
+int vk_pq_train_device(int device, const float* d_x, int64_t n, int d, int m, int64_t iters, uint64_t seed,
+                       float* centroids, void* stream) {
+    if (!d_x || !centroids) return fail(VK_ERR_INVALID, "pointers must not be NULL");
+    if (m <= 0 || d <= 0 || d % m != 0) return fail(VK_ERR_INVALID, "d must be a positive multiple of m");
+    if (n < vk::KSUB) return fail(VK_ERR_INVALID, "PQ training needs at least 256 vectors");
+    if (iters < 0) return fail(VK_ERR_INVALID, "iters must be >= 0");
+    const int dsub = d / m;
+    if (dsub > 128) return fail(VK_ERR_UNSUPPORTED, "dsub > 128 is not supported by the device trainer");
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t cbytes = (size_t)vk::KSUB * dsub * sizeof(float);
+    DevBuf<int> assign, counts;
+    DevBuf<float> cent, sums;
+    DevBuf<int64_t> rows;
+    VK_TRY(assign.ensure((size_t)n));
+    VK_TRY(counts.ensure(vk::KSUB));
+    VK_TRY(cent.ensure((size_t)vk::KSUB * dsub));
+    VK_TRY(sums.ensure((size_t)vk::KSUB * dsub));
+    VK_TRY(rows.ensure(vk::KSUB));
+    if (cbytes > 48 * 1024)
+        VK_TRY_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(&vk::train_assign_kernel),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cbytes));
+    // The reference's draws, in its order: one generator for the whole training, one shuffle of all row indices
+    // per sub-space (its first 256 entries seed the centroids), then rng() % n per empty cluster per iteration.
+    std::mt19937_64 rng(seed);
+    std::vector<size_t> perm((size_t)n);
+    std::vector<int64_t> host_rows(vk::KSUB);
+    std::vector<int> host_counts(vk::KSUB);
+    const unsigned agrid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 256), 148LL * 8));
+    for (int s = 0; s < m; ++s) {
+        std::iota(perm.begin(), perm.end(), (size_t)0);
+        std::shuffle(perm.begin(), perm.end(), rng);
+        for (int c = 0; c < vk::KSUB; ++c) host_rows[c] = (int64_t)perm[c];
+        VK_TRY_CUDA(cudaMemcpyAsync(rows.ptr, host_rows.data(), vk::KSUB * sizeof(int64_t), cudaMemcpyHostToDevice, st));
+        vk::train_gather_kernel<<<1, 256, 0, st>>>(d_x, d, s, dsub, rows.ptr, cent.ptr);
+        VK_TRY_CUDA(cudaGetLastError());
+        for (int64_t it = 0; it < iters; ++it) {
+            vk::train_assign_kernel<<<agrid, 256, cbytes, st>>>(d_x, n, d, s, dsub, cent.ptr, assign.ptr);
+            VK_TRY_CUDA(cudaGetLastError());
+            vk::train_sums_kernel<<<vk::KSUB / 8, 256, 0, st>>>(d_x, n, d, s, dsub, assign.ptr, sums.ptr, counts.ptr);
+            VK_TRY_CUDA(cudaGetLastError());
+            VK_TRY_CUDA(cudaMemcpyAsync(host_counts.data(), counts.ptr, vk::KSUB * sizeof(int), cudaMemcpyDeviceToHost,
+                                        st));
+            VK_TRY_CUDA(cudaStreamSynchronize(st));
+            for (int c = 0; c < vk::KSUB; ++c) host_rows[c] = host_counts[c] == 0 ? (int64_t)(rng() % (uint64_t)n) : 0;
+            VK_TRY_CUDA(cudaMemcpyAsync(rows.ptr, host_rows.data(), vk::KSUB * sizeof(int64_t), cudaMemcpyHostToDevice,
+                                        st));
+            vk::train_update_kernel<<<1, 256, 0, st>>>(d_x, d, s, dsub, sums.ptr, counts.ptr, rows.ptr, cent.ptr);
+            VK_TRY_CUDA(cudaGetLastError());
+        }
+        VK_TRY_CUDA(cudaMemcpyAsync(centroids + (size_t)s * vk::KSUB * dsub, cent.ptr, cbytes, cudaMemcpyDeviceToHost,
+                                    st));
+    }
+    VK_TRY_CUDA(cudaStreamSynchronize(st));
     return VK_OK;
 }
 

@@ -88,6 +88,27 @@ def gen_codes_rows(seed: int, cdf: np.ndarray, rows) -> np.ndarray:
     return out
 
 
+def pq_train_gpu(x, m: int, iters: int, seed: int = 1, device: int | None = None) -> np.ndarray:
+    """ProductQuantizer::train on the GPU (vk_pq_train_device): bit-identical centroids [m, 256, d/m]."""
+    import torch
+
+    from ._native import check, lib
+    dev = torch.cuda.current_device() if device is None else device
+    with torch.cuda.device(dev):
+        xs = x if isinstance(x, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(x, np.float32))
+        xs = xs.to(device=f"cuda:{dev}", dtype=torch.float32).contiguous()
+        n, d = xs.shape
+        cent = np.empty((m, 256, d // m), np.float32)
+        check(lib().vk_pq_train_device(dev, ptr(xs), n, d, m, iters, seed, ptr(cent),
+                                       torch.cuda.current_stream().cuda_stream), "pq_train")
+    return cent
+
+
+def gpu_trainer(device: int | None = None):
+    """train(x, m, iters, seed) -> centroids on the GPU (same result as pq_train)."""
+    return lambda x, m, iters, seed: pq_train_gpu(x, m, iters, seed, device)
+
+
 def gpu_encoder(device: int | None = None):
     """encode(centroids, x) -> codes on the GPU (vk_encode_device: bit-exact nearest centroid), 1M rows at a time."""
     def enc(cent, x):
