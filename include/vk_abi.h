@@ -128,6 +128,16 @@ int vk_index_info(const vk_index_t* index, int64_t* n, int* m, int* dsub, int64_
 /* Copies the index's row-major codes for rows [first, first + count) back to host memory (tests, tools). */
 int vk_index_get_codes(const vk_index_t* index, int64_t first, int64_t count, uint8_t* out);
 
+/* Persisted index (no counterpart in the reference, whose io.cpp only reads TEXMEX vectors). vk_index_save writes
+ * the index's centroids and its codes in row order to `path` (format in include/vk_host.h: header, centroids,
+ * row-major codes, one CRC-32C per 2^20 rows). vk_index_load builds an index on `device` from rows
+ * [row_first, row_first + count) of such a file (count < 0: to the end; id_base < 0: ids = file rows), reading
+ * only that range, so each shard of a multi-GPU search loads its own rows; verify != 0 checks every checksum block
+ * the range touches (VK_ERR_INVALID on a mismatch or a malformed file). */
+int vk_index_save(const vk_index_t* index, const char* path);
+int vk_index_load(int device, const char* path, int64_t row_first, int64_t count, int64_t id_base, int verify,
+                  vk_index_t** out);
+
 /* Lane placement of the device layout (no counterpart in the reference): out[j] = the row, relative to its window
  * of 64 positions, stored at position first + j, for j < count. The index stores the rows of every whole 64-row
  * window in an order chosen at build time to cut shared-memory bank conflicts of the LUT lookups; ids and results

@@ -14,6 +14,7 @@
 #ifndef VK_HOST_H
 #define VK_HOST_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -46,6 +47,25 @@ int vk_host_gen_codes(uint64_t seed, const uint32_t* cdf, int clusters, int m, i
 /* the listed rows (count of them, any order) of the generated code database (row-major count x m) */
 int vk_host_gen_codes_rows(uint64_t seed, const uint32_t* cdf, int clusters, int m, const int64_t* rows,
                            int64_t count, uint8_t* codes);
+
+/* ---- persisted index files (no counterpart in the reference, whose io.cpp only reads TEXMEX vectors) ----
+ * Format: 128-byte header ("VKPQIDX1", n, d, m, dsub, section offsets, CRC-32C of header and centroids), the
+ * centroids [m][256][dsub] fp32, the codes [n][m] uint8 row-major (4096-byte aligned), and one CRC-32C per block of
+ * 2^20 rows. Return 0, -1 for bad arguments, -2 for I/O or format errors (vk_host_last_error has the message). */
+int vk_host_last_error(char* buf, size_t len);
+
+/* CRC-32C (Castagnoli) of len bytes; hardware = 0 forces the portable table path. */
+uint32_t vk_host_crc32c(const void* data, size_t len, int hardware);
+
+/* Writes centroids [m][256][dsub] and codes [n][m] to `path`. */
+int vk_host_index_write(const char* path, const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n);
+
+/* Shape of the index in `path`; any pointer may be NULL. */
+int vk_host_index_info(const char* path, int64_t* n, int* d, int* m, int* dsub);
+
+/* Reads the centroids (if `centroids` is not NULL) and the codes of rows [first, first + count) of `path`. With
+ * verify != 0 every checksum block the range touches is read whole and checked. */
+int vk_host_index_read(const char* path, float* centroids, int64_t first, int64_t count, uint8_t* codes, int verify);
 
 #ifdef __cplusplus
 }

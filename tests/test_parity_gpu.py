@@ -369,6 +369,41 @@ def test_pq_train_device_reseeds_empty_clusters():
     assert np.array_equal(bits(host), bits(dev))
 
 
+def test_index_file_load_and_save(golden, tmp_path):
+    """vk_index_load (whole file, row ranges with file-row ids, verified) searches exactly like an index built from
+    the same arrays; vk_index_save writes the codes back in row order; damaged files are refused."""
+    from veckern_b200 import data
+    g = golden("gpu_fixture")
+    cent, codes, q = g["centroids"], g["codes"], g["queries"]
+    p = tmp_path / "fixture.vkpq"
+    data.write_index(p, cent, codes)
+    with PQSearcher(cent, codes) as ref, PQSearcher.load(p) as ld:
+        assert (ld.n, ld.m, ld.id_base) == (len(codes), codes.shape[1], 0)
+        assert np.array_equal(ld.get_codes(), codes)
+        a, _ = ref.search(q, 10)
+        b, _ = ld.search(q, 10)
+        assert np.array_equal(a.view(np.int64), b.view(np.int64))
+    lo, hi = 7_001, 19_999
+    with PQSearcher(cent, codes[lo:hi], id_base=lo) as ref, PQSearcher.load(p, rows=(lo, hi)) as ld:
+        assert ld.id_base == lo
+        a, _ = ref.search(q, 33)
+        b, _ = ld.search(q, 33)
+        assert np.array_equal(a.view(np.int64), b.view(np.int64))
+    p2 = tmp_path / "saved.vkpq"
+    with PQSearcher(cent, codes) as s:
+        s.save(p2)
+    c2, k2 = data.read_index(p2)
+    assert np.array_equal(c2, cent) and np.array_equal(k2, codes)
+    raw = bytearray(p.read_bytes())
+    raw[int.from_bytes(raw[48:56], "little") + 99] ^= 1
+    bad = tmp_path / "bad.vkpq"
+    bad.write_bytes(bytes(raw))
+    with pytest.raises(VkError, match="checksum"):
+        PQSearcher.load(bad)
+    with pytest.raises(VkError):
+        PQSearcher.load(p, rows=(0, len(codes) + 1))
+
+
 def test_rerank_kernel_matches_reference(golden, port):
     """GPU exact re-rank == the reference's rerank_exact (fixture) and the oracle (duplicates, padding, ties)."""
     import torch

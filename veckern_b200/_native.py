@@ -70,6 +70,8 @@ ABI = {
                                 C.POINTER(C.c_int)]),
     "vk_index_get_codes": (C.c_int, [_vp, _i64, _i64, _vp]),
     "vk_index_get_placement": (C.c_int, [_vp, _i64, _i64, _vp]),
+    "vk_index_save": (C.c_int, [_vp, C.c_char_p]),
+    "vk_index_load": (C.c_int, [C.c_int, C.c_char_p, _i64, _i64, _i64, C.c_int, C.POINTER(_vp)]),
     "vk_search": (C.c_int, [_vp, _vp, _i64, C.c_int, C.c_int, C.POINTER(Tuning), _vp, C.POINTER(Timings),
                             C.POINTER(LaunchShape)]),
     "vk_search_device": (C.c_int, [_vp, _vp, _i64, C.c_int, C.POINTER(Tuning), _vp, _vp]),
@@ -95,6 +97,12 @@ HOST_ABI = {
     "vk_host_gen_cdf": (C.c_int, [_u64, C.c_int, C.c_int, C.c_double, _vp]),
     "vk_host_gen_codes": (C.c_int, [_u64, _vp, C.c_int, C.c_int, _i64, _i64, _vp]),
     "vk_host_gen_codes_rows": (C.c_int, [_u64, _vp, C.c_int, C.c_int, _vp, _i64, _vp]),
+    "vk_host_last_error": (C.c_int, [C.c_char_p, C.c_size_t]),
+    "vk_host_crc32c": (C.c_uint32, [_vp, C.c_size_t, C.c_int]),
+    "vk_host_index_write": (C.c_int, [C.c_char_p, _vp, C.c_int, C.c_int, _vp, _i64]),
+    "vk_host_index_info": (C.c_int, [C.c_char_p, C.POINTER(_i64), C.POINTER(C.c_int), C.POINTER(C.c_int),
+                                     C.POINTER(C.c_int)]),
+    "vk_host_index_read": (C.c_int, [C.c_char_p, _vp, _i64, _i64, _vp, C.c_int]),
 }
 
 _lib = None

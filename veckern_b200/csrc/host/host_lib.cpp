@@ -9,12 +9,15 @@
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
+#include <string>
 #include <numeric>
 #include <random>
 #include <vector>
 
 #include "../vk_gen.h"
+#include "index_file.h"
 #include "veckern/pq.hpp"
 #include "vk_host.h"
 
@@ -274,3 +277,59 @@ int vk_host_gen_codes_rows(uint64_t seed, const uint32_t* cdf, int clusters, int
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------ index files
+namespace {
+thread_local std::string g_host_error;
+int host_fail(int code, const std::string& msg) {
+    g_host_error = msg;
+    return code;
+}
+}  // namespace
+
+int vk_host_last_error(char* buf, size_t len) {
+    if (!buf || len == 0) return -1;
+    std::snprintf(buf, len, "%s", g_host_error.c_str());
+    return 0;
+}
+
+uint32_t vk_host_crc32c(const void* data, size_t len, int hardware) { return vkio::crc32c(data, len, hardware != 0); }
+
+int vk_host_index_write(const char* path, const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n) {
+    if (!path || !centroids || (!codes && n > 0) || m <= 0 || dsub <= 0 || n < 0) return host_fail(-1, "bad arguments");
+    uint64_t done = 0;
+    const std::string err = vkio::write_index(path, centroids, (uint32_t)m, (uint32_t)dsub, (uint64_t)n,
+                                              [&](uint64_t rows, uint8_t* buf) {
+                                                  std::memcpy(buf, codes + done * m, rows * m);
+                                                  done += rows;
+                                                  return true;
+                                              });
+    return err.empty() ? 0 : host_fail(-2, err);
+}
+
+int vk_host_index_info(const char* path, int64_t* n, int* d, int* m, int* dsub) {
+    if (!path) return host_fail(-1, "bad arguments");
+    vkio::Reader r(path);
+    if (!r.ok()) return host_fail(-2, r.err);
+    if (n) *n = (int64_t)r.h.n;
+    if (d) *d = (int)r.h.d;
+    if (m) *m = (int)r.h.m;
+    if (dsub) *dsub = (int)r.h.dsub;
+    return 0;
+}
+
+int vk_host_index_read(const char* path, float* centroids, int64_t first, int64_t count, uint8_t* codes, int verify) {
+    if (!path || first < 0 || count < 0 || (!codes && count > 0)) return host_fail(-1, "bad arguments");
+    vkio::Reader r(path);
+    if (!r.ok()) return host_fail(-2, r.err);
+    if (centroids) {
+        const std::string err = r.centroids(centroids);
+        if (!err.empty()) return host_fail(-2, err);
+    }
+    const std::string err = r.rows((uint64_t)first, (uint64_t)count, verify != 0,
+                                   [&](uint64_t row0, uint64_t rows, const uint8_t* bytes) {
+                                       std::memcpy(codes + (row0 - first) * r.h.m, bytes, rows * r.h.m);
+                                       return true;
+                                   });
+    return err.empty() ? 0 : host_fail(err == "row range out of bounds" ? -1 : -2, err);
+}

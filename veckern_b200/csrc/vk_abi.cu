@@ -21,6 +21,7 @@
 
 #include "../../include/vk_abi.h"
 #include "aux_kernels.cuh"
+#include "host/index_file.h"
 #include "kernels.cuh"
 #include "scan_dispatch.cuh"
 
@@ -620,6 +621,96 @@ int vk_index_get_codes(const vk_index_t* ix, int64_t first, int64_t count, uint8
     if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);
     cudaFree(d);
     if (e != cudaSuccess) return fail(VK_ERR_CUDA, "reading codes failed: %s", cudaGetErrorString(e));
+    return VK_OK;
+}
+
+int vk_index_save(const vk_index_t* ix, const char* path) {
+    if (!ix || !path) return fail(VK_ERR_INVALID, "index and path must not be NULL");
+    DeviceGuard guard(ix->device);
+    std::vector<float> cent((size_t)ix->m * vk::KSUB * ix->dsub);
+    VK_TRY_CUDA(cudaMemcpy(cent.data(), ix->centroids, cent.size() * sizeof(float), cudaMemcpyDeviceToHost));
+    int64_t done = 0;
+    int rc = VK_OK;
+    const std::string err = vkio::write_index(path, cent.data(), (uint32_t)ix->m, (uint32_t)ix->dsub, (uint64_t)ix->n,
+                                              [&](uint64_t rows, uint8_t* buf) {
+                                                  rc = vk_index_get_codes(ix, done, (int64_t)rows, buf);
+                                                  done += (int64_t)rows;
+                                                  return rc == VK_OK;
+                                              });
+    if (rc != VK_OK) return rc;
+    if (!err.empty()) return fail(VK_ERR_CUDA, "saving %s: %s", path, err.c_str());
+    return VK_OK;
+}
+
+int vk_index_load(int device, const char* path, int64_t row_first, int64_t count, int64_t id_base, int verify,
+                  vk_index_t** out) {
+    if (!path || !out) return fail(VK_ERR_INVALID, "path and out must not be NULL");
+    *out = nullptr;
+    vkio::Reader rd(path);
+    if (!rd.ok()) return fail(VK_ERR_INVALID, "%s: %s", path, rd.err.c_str());
+    const int64_t n_file = (int64_t)rd.h.n;
+    if (count < 0) count = n_file - row_first;
+    if (row_first < 0 || row_first > n_file || count <= 0 || count > n_file - row_first)
+        return fail(VK_ERR_INVALID, "row range [%lld, +%lld) is outside the file's %lld rows", (long long)row_first,
+                    (long long)count, (long long)n_file);
+    if (id_base < 0) id_base = row_first;
+    std::vector<float> cent((size_t)rd.h.m * vk::KSUB * rd.h.dsub);
+    std::string err = rd.centroids(cent.data());
+    if (!err.empty()) return fail(VK_ERR_INVALID, "%s: %s", path, err.c_str());
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(guard.err));
+    vk_index* ix = nullptr;
+    int rc = create_common(device, cent.data(), (int)rd.h.m, (int)rd.h.dsub, count, id_base, out, ix);
+    if (rc != VK_OK) {
+        delete ix;
+        return rc;
+    }
+    // Rows arrive in pieces of at most one checksum block; they are gathered into a staging slice (a multiple of
+    // 32 rows, so every slice starts a 32-row group) and interleaved on the device slice by slice.
+    const int m = ix->m;
+    const int64_t slice = std::min<int64_t>(ceil_div(count, 32) * 32, int64_t(1) << 22);
+    std::vector<uint8_t> host((size_t)slice * m);
+    uint8_t* staging = nullptr;
+    cudaError_t e = cudaMalloc(&staging, (size_t)slice * m);
+    int64_t fill = 0, slice0 = 0;  // rows in the staging slice, its first row (relative to row_first)
+    auto flush = [&]() {
+        if (e != cudaSuccess || fill == 0) return;
+        e = cudaMemcpyAsync(staging, host.data(), (size_t)fill * m, cudaMemcpyHostToDevice, ix->stream);
+        if (e == cudaSuccess) {
+            vk::interleave_kernel<<<grid_for(ceil_div(fill, 32) * 32 * ix->W, ix->sm_count), 256, 0, ix->stream>>>(
+                staging, slice0, fill, count, m, ix->W, ix->codes);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);  // host and staging are reused
+        slice0 += fill;
+        fill = 0;
+    };
+    if (e == cudaSuccess) {
+        err = rd.rows((uint64_t)row_first, (uint64_t)count, verify != 0,
+                      [&](uint64_t row0, uint64_t rows, const uint8_t* bytes) {
+                          uint64_t done = 0;
+                          while (done < rows && e == cudaSuccess) {
+                              const int64_t take = std::min<int64_t>((int64_t)(rows - done), slice - fill);
+                              std::memcpy(host.data() + (size_t)fill * m, bytes + done * m, (size_t)take * m);
+                              fill += take;
+                              done += (uint64_t)take;
+                              if (fill == slice) flush();
+                          }
+                          (void)row0;
+                          return e == cudaSuccess;
+                      });
+        flush();
+    }
+    if (staging) cudaFree(staging);
+    if (e == cudaSuccess && err.empty()) e = place_rows(ix);
+    if (e == cudaSuccess && err.empty()) e = cudaStreamSynchronize(ix->stream);
+    if (e != cudaSuccess || !err.empty()) {
+        delete ix;
+        *out = nullptr;
+        if (!err.empty()) return fail(VK_ERR_INVALID, "%s: %s", path, err.c_str());
+        return fail(VK_ERR_CUDA, "loading %s failed: %s", path, cudaGetErrorString(e));
+    }
+    *out = ix;
     return VK_OK;
 }
 

@@ -129,3 +129,54 @@ def gpu_encoder(device: int | None = None):
                 out[a:a + xs.shape[0]] = cs.cpu().numpy()
         return out
     return enc
+
+
+# ---------------------------------------------------------------------------------------------- index files
+class IndexFileError(IOError):
+    pass
+
+
+def _host_check(rc: int, what: str) -> None:
+    if rc != 0:
+        import ctypes as C
+        buf = C.create_string_buffer(1024)
+        host().vk_host_last_error(buf, len(buf))
+        msg = buf.value.decode(errors="replace")
+        if rc == -1:
+            raise ValueError(f"{what}: {msg}")
+        raise IndexFileError(f"{what}: {msg}")
+
+
+def crc32c(data, hardware: bool = True) -> int:
+    a = np.ascontiguousarray(np.frombuffer(data, np.uint8) if isinstance(data, (bytes, bytearray)) else data)
+    return int(host().vk_host_crc32c(ptr(a), a.nbytes, int(hardware)))
+
+
+def write_index(path, centroids: np.ndarray, codes: np.ndarray) -> None:
+    """Persisted index file: centroids [m, 256, dsub] fp32 + codes [n, m] uint8 (format in include/vk_host.h)."""
+    centroids = np.ascontiguousarray(centroids, np.float32)
+    codes = np.ascontiguousarray(codes, np.uint8)
+    m, _, dsub = centroids.shape
+    if codes.ndim != 2 or codes.shape[1] != m:
+        raise ValueError("codes must be [n, m] uint8")
+    _host_check(host().vk_host_index_write(str(path).encode(), ptr(centroids), m, dsub, ptr(codes), codes.shape[0]),
+                "write_index")
+
+
+def index_info(path) -> dict:
+    import ctypes as C
+    n, d, m, dsub = C.c_int64(), C.c_int(), C.c_int(), C.c_int()
+    _host_check(host().vk_host_index_info(str(path).encode(), C.byref(n), C.byref(d), C.byref(m), C.byref(dsub)),
+                "index_info")
+    return {"n": n.value, "d": d.value, "m": m.value, "dsub": dsub.value}
+
+
+def read_index(path, rows: tuple[int, int] | None = None, verify: bool = True):
+    """(centroids [m, 256, dsub], codes of rows [lo, hi)) of a persisted index file; only that range is read."""
+    info = index_info(path)
+    lo, hi = rows if rows is not None else (0, info["n"])
+    cent = np.empty((info["m"], 256, info["dsub"]), np.float32)
+    codes = np.empty((max(0, hi - lo), info["m"]), np.uint8)
+    _host_check(host().vk_host_index_read(str(path).encode(), ptr(cent), lo, hi - lo, ptr(codes), int(verify)),
+                "read_index")
+    return cent, codes

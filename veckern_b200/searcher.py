@@ -147,6 +147,22 @@ class PQSearcher:
                                               row_first, n, id_base, C.byref(h)), "vk_index_create_generated")
         return cls(None, _handle=h)
 
+    @classmethod
+    def load(cls, path: str, *, rows: tuple[int, int] | None = None, id_base: int | None = None, device: int = 0,
+             verify: bool = True) -> "PQSearcher":
+        """An index built from rows [lo, hi) (default: all) of a persisted index file (vk_index_load); ids default
+        to the file's row numbers. Reads only that range: each shard of a multi-GPU search loads its own rows."""
+        lo, hi = rows if rows is not None else (0, -1)
+        h = C.c_void_p()
+        count = -1 if hi < 0 else hi - lo
+        check(lib().vk_index_load(device, str(path).encode(), lo, count, -1 if id_base is None else id_base,
+                                  int(verify), C.byref(h)), "vk_index_load")
+        return cls(None, _handle=h)
+
+    def save(self, path: str) -> None:
+        """Writes the centroids and the codes (row order) to a persisted index file (vk_index_save)."""
+        check(lib().vk_index_save(self._h, str(path).encode()), "vk_index_save")
+
     def close(self) -> None:
         if self._h:
             lib().vk_index_destroy(self._h)
