@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <memory>
 #include <string>
+#include <vector>
 
 #include "veckern/common.hpp"
 #include "veckern/pq.hpp"
@@ -76,6 +77,26 @@ public:
         double waves = 0.0;
     };
     LaunchShape last_launch() const;
+
+private:
+    struct Impl;
+    std::unique_ptr<Impl> impl_;
+};
+
+// Additive (no counterpart in the reference): one database split into contiguous row shards over several devices
+// of this process (a device may be listed more than once); search results are identical to one PQSearcher over all
+// rows. Backed by vk_multi_* of include/vk_abi.h.
+class MultiPQSearcher {
+public:
+    MultiPQSearcher(const ProductQuantizer& pq, const uint8_t* codes, std::size_t n, const std::vector<int>& devices);
+    ~MultiPQSearcher();
+    MultiPQSearcher(const MultiPQSearcher&) = delete;
+    MultiPQSearcher& operator=(const MultiPQSearcher&) = delete;
+
+    // out: nq x k neighbors, ascending (dist, id), global row ids. 1 <= k <= min(128, n).
+    Timings search(const float* queries, std::size_t nq, std::size_t k, Neighbor* out);
+    void set_tuning(const Tuning& tuning);
+    std::size_t shards() const;
 
 private:
     struct Impl;

@@ -128,6 +128,21 @@ int vk_index_info(const vk_index_t* index, int64_t* n, int* m, int* dsub, int64_
 /* Copies the index's row-major codes for rows [first, first + count) back to host memory (tests, tools). */
 int vk_index_get_codes(const vk_index_t* index, int64_t first, int64_t count, uint8_t* out);
 
+/* Single-process multi-GPU search (no counterpart in the reference, which runs on one device). The database is
+ * split into ndev contiguous row shards, shard g on devices[g] (a device may be listed more than once) with global
+ * ids; vk_multi_search runs every shard on its own stream, gathers the per-shard lists on devices[0] over the
+ * device interconnect and merges them there: results are identical to one index over all rows. Timings:
+ * scan_ms = slowest shard (LUT + scan + its lists), select_ms = cross-shard merge, transfer_ms = the rest. */
+typedef struct vk_multi vk_multi_t;
+int vk_multi_create(int ndev, const int* devices, const float* centroids, int m, int dsub, const uint8_t* codes,
+                    int64_t n, vk_multi_t** out);
+/* Each shard reads only its rows of a persisted index file (vk_index_load). */
+int vk_multi_load(int ndev, const int* devices, const char* path, int verify, vk_multi_t** out);
+int vk_multi_search(vk_multi_t* multi, const float* queries, int64_t nq, int k, const vk_tuning_t* tuning,
+                    vk_neighbor_t* out, vk_timings_t* timings);
+int vk_multi_info(const vk_multi_t* multi, int64_t* n, int* shards);
+int vk_multi_destroy(vk_multi_t* multi);
+
 /* Persisted index (no counterpart in the reference, whose io.cpp only reads TEXMEX vectors). vk_index_save writes
  * the index's centroids and its codes in row order to `path` (format in include/vk_host.h: header, centroids,
  * row-major codes, one CRC-32C per 2^20 rows). vk_index_load builds an index on `device` from rows

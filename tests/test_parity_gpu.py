@@ -404,6 +404,39 @@ def test_index_file_load_and_save(golden, tmp_path):
         PQSearcher.load(p, rows=(0, len(codes) + 1))
 
 
+@pytest.mark.parametrize("devices,k", [([0, 0, 0], 10), ([0, 0], 128), ([0] * 5, 33)])
+def test_multi_gpu_searcher_matches_one_index(golden, devices, k):
+    """vk_multi_* (shards listed on the one device here; each shard on its own stream, lists gathered with
+    cudaMemcpyPeerAsync and merged) == one index over all rows."""
+    from veckern_b200 import MultiPQSearcher
+    g = golden("gpu_fixture")
+    cent, codes, q = g["centroids"], g["codes"], g["queries"]
+    with PQSearcher(cent, codes) as one, MultiPQSearcher(cent, codes, devices=devices) as mx:
+        assert (mx.n, mx.shards) == (len(codes), len(devices))
+        a, _ = one.search(q, k)
+        b, t = mx.search(q, k)
+        assert np.array_equal(a.view(np.int64), b.view(np.int64))
+        assert t.scan_ms > 0
+
+
+def test_multi_gpu_searcher_pads_small_shards_and_loads(tmp_path):
+    """Shards with fewer than k rows (their lists padded for the merge), and shards loaded from one index file."""
+    from veckern_b200 import MultiPQSearcher, data
+    cent, codes, q = random_db(21, 301, 16, 8, 9, dup_rows=40)
+    with PQSearcher(cent, codes) as one:
+        a, _ = one.search(q, 100)
+    with MultiPQSearcher(cent, codes, devices=[0, 0, 0, 0]) as mx:
+        b, _ = mx.search(q, 100)
+    assert np.array_equal(a.view(np.int64), b.view(np.int64))
+    p = tmp_path / "db.vkpq"
+    data.write_index(p, cent, codes)
+    with MultiPQSearcher.load(p, devices=[0, 0, 0]) as mx:
+        c, _ = mx.search(q, 100)
+    assert np.array_equal(a.view(np.int64), c.view(np.int64))
+    with pytest.raises(VkError):
+        MultiPQSearcher(cent, codes[:3], devices=[0] * 4)
+
+
 def test_rerank_kernel_matches_reference(golden, port):
     """GPU exact re-rank == the reference's rerank_exact (fixture) and the oracle (duplicates, padding, ties)."""
     import torch

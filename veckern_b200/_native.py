@@ -71,6 +71,11 @@ ABI = {
     "vk_index_get_codes": (C.c_int, [_vp, _i64, _i64, _vp]),
     "vk_index_get_placement": (C.c_int, [_vp, _i64, _i64, _vp]),
     "vk_index_save": (C.c_int, [_vp, C.c_char_p]),
+    "vk_multi_create": (C.c_int, [C.c_int, _vp, _vp, C.c_int, C.c_int, _vp, _i64, C.POINTER(_vp)]),
+    "vk_multi_load": (C.c_int, [C.c_int, _vp, C.c_char_p, C.c_int, C.POINTER(_vp)]),
+    "vk_multi_search": (C.c_int, [_vp, _vp, _i64, C.c_int, C.POINTER(Tuning), _vp, C.POINTER(Timings)]),
+    "vk_multi_info": (C.c_int, [_vp, C.POINTER(_i64), C.POINTER(C.c_int)]),
+    "vk_multi_destroy": (C.c_int, [_vp]),
     "vk_index_load": (C.c_int, [C.c_int, C.c_char_p, _i64, _i64, _i64, C.c_int, C.POINTER(_vp)]),
     "vk_search": (C.c_int, [_vp, _vp, _i64, C.c_int, C.c_int, C.POINTER(Tuning), _vp, C.POINTER(Timings),
                             C.POINTER(LaunchShape)]),

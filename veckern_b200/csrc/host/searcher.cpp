@@ -118,4 +118,46 @@ Timings PQSearcher::distances(const float* queries, std::size_t nq, ScanVariant 
     return Timings{t.transfer_ms, t.lut_ms, t.scan_ms, t.select_ms};
 }
 
+struct MultiPQSearcher::Impl {
+    vk_multi_t* multi = nullptr;
+    std::size_t n = 0, shards = 0;
+    Tuning tuning;
+    ~Impl() {
+        if (multi) vk_multi_destroy(multi);
+    }
+};
+
+MultiPQSearcher::MultiPQSearcher(const ProductQuantizer& pq, const uint8_t* codes, std::size_t n,
+                                 const std::vector<int>& devices)
+    : impl_(std::make_unique<Impl>()) {
+    check(n > 0 && n < static_cast<std::size_t>(2147483647), "n must fit in int32 ids");
+    check(!devices.empty(), "need at least one device");
+    impl_->n = n;
+    impl_->shards = devices.size();
+    ok(vk_multi_create(static_cast<int>(devices.size()), devices.data(), pq.centroids().data(),
+                       static_cast<int>(pq.m()), static_cast<int>(pq.dsub()), codes, static_cast<int64_t>(n),
+                       &impl_->multi),
+       "vk_multi_create");
+}
+
+MultiPQSearcher::~MultiPQSearcher() = default;
+
+void MultiPQSearcher::set_tuning(const Tuning& t) {
+    const vk_tuning_t c = to_c(t);
+    ok(vk_tuning_validate(&c), "set_tuning");
+    impl_->tuning = t;
+}
+
+std::size_t MultiPQSearcher::shards() const { return impl_->shards; }
+
+Timings MultiPQSearcher::search(const float* queries, std::size_t nq, std::size_t k, Neighbor* out) {
+    check(k >= 1 && k <= 128 && k <= impl_->n, "k must be in [1, min(128, n)]");
+    const vk_tuning_t c = to_c(impl_->tuning);
+    vk_timings_t t{};
+    ok(vk_multi_search(impl_->multi, queries, static_cast<int64_t>(nq), static_cast<int>(k), &c,
+                       reinterpret_cast<vk_neighbor_t*>(out), &t),
+       "multi search");
+    return Timings{t.transfer_ms, t.lut_ms, t.scan_ms, t.select_ms};
+}
+
 }  // namespace veckern::gpu

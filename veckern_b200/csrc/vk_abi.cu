@@ -714,6 +714,222 @@ int vk_index_load(int device, const char* path, int64_t row_first, int64_t count
     return VK_OK;
 }
 
+// ------------------------------------------------------------------------------------------------ multi-GPU
+}  // extern "C"
+
+// One process, several devices: shard g of G holds rows [g * ceil(n / G), ...) as its own index with global ids.
+// A search launches every shard's search on its own stream (all asynchronous, so the devices run concurrently from
+// one host thread), pads each shard's lists to k when the shard has fewer than k rows, copies them over the device
+// interconnect (cudaMemcpyPeerAsync) into a [shard][query][k] buffer on the first device and merges them there.
+struct vk_multi {
+    struct Lane {
+        int device = 0;
+        vk_index* index = nullptr;
+        int64_t lo = 0, rows = 0;
+        cudaStream_t st = nullptr;
+        cudaEvent_t ev[3] = {};  // before the search, after it, after the copy to the first device
+        DevBuf<float> queries;
+        DevBuf<int2> res, padded;
+    };
+    std::vector<Lane> lanes;
+    int64_t n = 0;
+    int m = 0, dsub = 0;
+    cudaStream_t st0 = nullptr;  // on lanes[0].device
+    cudaEvent_t ev0[4] = {};
+    DevBuf<int2> lists, merged;
+
+    ~vk_multi() {
+        for (auto& l : lanes) {
+            DeviceGuard g(l.device);
+            delete l.index;
+            l.index = nullptr;
+            l.queries.release();
+            l.res.release();
+            l.padded.release();
+            for (auto& e : l.ev)
+                if (e) cudaEventDestroy(e);
+            if (l.st) cudaStreamDestroy(l.st);
+        }
+        if (!lanes.empty()) {
+            DeviceGuard g(lanes[0].device);
+            lists.release();
+            merged.release();
+            for (auto& e : ev0)
+                if (e) cudaEventDestroy(e);
+            if (st0) cudaStreamDestroy(st0);
+        }
+    }
+};
+
+namespace {
+
+// Creates the lanes' streams and events, enables peer access to the first device; `make(lane)` builds the index.
+template <class Make>
+int multi_create(int ndev, const int* devices, int64_t n, vk_multi_t** out, Make&& make) {
+    if (!out) return fail(VK_ERR_INVALID, "out must not be NULL");
+    *out = nullptr;
+    if (ndev < 1 || !devices) return fail(VK_ERR_INVALID, "need at least one device");
+    const int64_t per = ceil_div(n, ndev);
+    if (n <= 0 || (int64_t)(ndev - 1) * per >= n)
+        return fail(VK_ERR_INVALID, "n = %lld rows leave a shard of %d empty", (long long)n, ndev);
+    auto* mx = new vk_multi();
+    mx->n = n;
+    mx->lanes.resize(ndev);
+    int rc = VK_OK;
+    for (int g = 0; g < ndev && rc == VK_OK; ++g) {
+        auto& l = mx->lanes[g];
+        l.device = devices[g];
+        l.lo = (int64_t)g * per;
+        l.rows = std::min(n, l.lo + per) - l.lo;
+        rc = make(l);
+        if (rc != VK_OK) break;
+        DeviceGuard guard(l.device);
+        if (cudaStreamCreateWithFlags(&l.st, cudaStreamNonBlocking) != cudaSuccess) rc = fail(VK_ERR_CUDA, "stream");
+        for (auto& e : l.ev)
+            if (rc == VK_OK && cudaEventCreate(&e) != cudaSuccess) rc = fail(VK_ERR_CUDA, "event");
+        if (rc == VK_OK && l.device != devices[0]) {
+            int can = 0;
+            cudaDeviceCanAccessPeer(&can, devices[0], l.device);
+            if (can) {
+                DeviceGuard g0(devices[0]);
+                const cudaError_t e = cudaDeviceEnablePeerAccess(l.device, 0);
+                if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
+                    rc = fail(VK_ERR_CUDA, "peer access %d -> %d: %s", devices[0], l.device, cudaGetErrorString(e));
+                cudaGetLastError();  // clear cudaErrorPeerAccessAlreadyEnabled
+            }
+        }
+    }
+    if (rc == VK_OK) {
+        mx->m = mx->lanes[0].index->m;
+        mx->dsub = mx->lanes[0].index->dsub;
+        DeviceGuard guard(devices[0]);
+        if (cudaStreamCreateWithFlags(&mx->st0, cudaStreamNonBlocking) != cudaSuccess) rc = fail(VK_ERR_CUDA, "stream");
+        for (auto& e : mx->ev0)
+            if (rc == VK_OK && cudaEventCreate(&e) != cudaSuccess) rc = fail(VK_ERR_CUDA, "event");
+    }
+    if (rc != VK_OK) {
+        delete mx;
+        return rc;
+    }
+    *out = mx;
+    return VK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int vk_multi_create(int ndev, const int* devices, const float* centroids, int m, int dsub, const uint8_t* codes,
+                    int64_t n, vk_multi_t** out) {
+    if (!codes || !centroids) return fail(VK_ERR_INVALID, "centroids and codes must not be NULL");
+    return multi_create(ndev, devices, n, out, [&](vk_multi::Lane& l) {
+        return vk_index_create(l.device, centroids, m, dsub, codes + l.lo * m, l.rows, l.lo, &l.index);
+    });
+}
+
+int vk_multi_load(int ndev, const int* devices, const char* path, int verify, vk_multi_t** out) {
+    if (!path) return fail(VK_ERR_INVALID, "path must not be NULL");
+    vkio::Reader rd(path);
+    if (!rd.ok()) return fail(VK_ERR_INVALID, "%s: %s", path, rd.err.c_str());
+    return multi_create(ndev, devices, (int64_t)rd.h.n, out, [&](vk_multi::Lane& l) {
+        return vk_index_load(l.device, path, l.lo, l.rows, l.lo, verify, &l.index);
+    });
+}
+
+int vk_multi_destroy(vk_multi_t* mx) {
+    delete mx;
+    return VK_OK;
+}
+
+int vk_multi_info(const vk_multi_t* mx, int64_t* n, int* shards) {
+    if (!mx) return fail(VK_ERR_INVALID, "multi-GPU searcher must not be NULL");
+    if (n) *n = mx->n;
+    if (shards) *shards = (int)mx->lanes.size();
+    return VK_OK;
+}
+
+int vk_multi_search(vk_multi_t* mx, const float* queries, int64_t nq, int k, const vk_tuning_t* tuning,
+                    vk_neighbor_t* out, vk_timings_t* timings) {
+    if (!mx) return fail(VK_ERR_INVALID, "multi-GPU searcher must not be NULL");
+    if (k < 1 || k > 128 || (int64_t)k > mx->n) return fail(VK_ERR_INVALID, "k must be in [1, min(128, n)]");
+    if (nq < 0) return fail(VK_ERR_INVALID, "nq must be >= 0");
+    if (nq > 0 && (!queries || !out)) return fail(VK_ERR_INVALID, "queries and out must not be NULL");
+    vk_tuning_t t;
+    vk_tuning_default(&t);
+    if (tuning) t = *tuning;
+    VK_TRY(validate_tuning(&t));
+    if (timings) *timings = vk_timings_t{};
+    if (nq == 0) return VK_OK;
+    const int G = (int)mx->lanes.size();
+    const int d = mx->m * mx->dsub;
+    int64_t batch = nq;
+    for (auto& l : mx->lanes) batch = std::min(batch, max_query_batch(l.index));
+    const int dev0 = mx->lanes[0].device;
+    vk_timings_t acc{};
+    for (int64_t q0 = 0; q0 < nq; q0 += batch) {
+        const int64_t b = std::min(batch, nq - q0);
+        {
+            DeviceGuard g0(dev0);
+            VK_TRY(mx->lists.ensure((size_t)G * b * k));
+            VK_TRY(mx->merged.ensure((size_t)b * k));
+            VK_TRY_CUDA(cudaEventRecord(mx->ev0[0], mx->st0));
+        }
+        for (int g = 0; g < G; ++g) {
+            auto& l = mx->lanes[g];
+            DeviceGuard guard(l.device);
+            const int kg = (int)std::min<int64_t>(k, l.rows);
+            VK_TRY(l.queries.ensure((size_t)b * d));
+            VK_TRY(l.res.ensure((size_t)b * kg));
+            VK_TRY_CUDA(cudaMemcpyAsync(l.queries.ptr, queries + q0 * d, (size_t)b * d * sizeof(float),
+                                        cudaMemcpyHostToDevice, l.st));
+            VK_TRY_CUDA(cudaEventRecord(l.ev[0], l.st));
+            VK_TRY(run_search(l.index, l.queries.ptr, b, kg, t, l.res.ptr, l.st, nullptr, nullptr));
+            VK_TRY_CUDA(cudaEventRecord(l.ev[1], l.st));
+            const int2* src = l.res.ptr;
+            if (kg < k) {  // a shard with fewer than k rows: pad its lists with (NaN bits, -1) = merge padding
+                VK_TRY(l.padded.ensure((size_t)b * k));
+                VK_TRY_CUDA(cudaMemsetAsync(l.padded.ptr, 0xFF, (size_t)b * k * sizeof(int2), l.st));
+                VK_TRY_CUDA(cudaMemcpy2DAsync(l.padded.ptr, (size_t)k * sizeof(int2), l.res.ptr,
+                                              (size_t)kg * sizeof(int2), (size_t)kg * sizeof(int2), (size_t)b,
+                                              cudaMemcpyDeviceToDevice, l.st));
+                src = l.padded.ptr;
+            }
+            VK_TRY_CUDA(cudaMemcpyPeerAsync(mx->lists.ptr + (size_t)g * b * k, dev0, src, l.device,
+                                            (size_t)b * k * sizeof(int2), l.st));
+            VK_TRY_CUDA(cudaEventRecord(l.ev[2], l.st));
+        }
+        DeviceGuard g0(dev0);
+        for (auto& l : mx->lanes) VK_TRY_CUDA(cudaStreamWaitEvent(mx->st0, l.ev[2], 0));
+        VK_TRY_CUDA(cudaEventRecord(mx->ev0[1], mx->st0));
+        VK_TRY(vk_merge_topk_device(dev0, reinterpret_cast<const vk_neighbor_t*>(mx->lists.ptr), b, G, k, k, b * k,
+                                    k, reinterpret_cast<vk_neighbor_t*>(mx->merged.ptr), mx->st0));
+        VK_TRY_CUDA(cudaEventRecord(mx->ev0[2], mx->st0));
+        VK_TRY_CUDA(cudaMemcpyAsync(out + q0 * k, mx->merged.ptr, (size_t)b * k * sizeof(int2), cudaMemcpyDeviceToHost,
+                                    mx->st0));
+        VK_TRY_CUDA(cudaEventRecord(mx->ev0[3], mx->st0));
+        VK_TRY_CUDA(cudaEventSynchronize(mx->ev0[3]));
+        float scan = 0.f, ms = 0.f;
+        for (auto& l : mx->lanes) {
+            DeviceGuard guard(l.device);
+            VK_TRY_CUDA(cudaEventElapsedTime(&ms, l.ev[0], l.ev[1]));
+            scan = std::max(scan, ms);
+        }
+        float gather_merge = 0.f, copy_out = 0.f, total = 0.f;
+        VK_TRY_CUDA(cudaEventElapsedTime(&gather_merge, mx->ev0[1], mx->ev0[2]));
+        VK_TRY_CUDA(cudaEventElapsedTime(&copy_out, mx->ev0[2], mx->ev0[3]));
+        VK_TRY_CUDA(cudaEventElapsedTime(&total, mx->ev0[0], mx->ev0[3]));
+        acc.scan_ms += scan;                                                  // slowest shard: LUT + scan + lists
+        acc.select_ms += gather_merge;                                        // cross-shard merge on the first device
+        acc.transfer_ms += std::max(0.f, total - scan - gather_merge);        // query uploads, gathers, result copy
+    }
+    for (auto& l : mx->lanes) {
+        DeviceGuard guard(l.device);
+        VK_TRY(read_status(l.index, l.st));
+    }
+    if (timings) *timings = acc;
+    return VK_OK;
+}
+
 int vk_index_get_placement(const vk_index_t* ix, int64_t first, int64_t count, uint8_t* out) {
     if (!ix || (!out && count > 0)) return fail(VK_ERR_INVALID, "index and out must not be NULL");
     if (first < 0 || count < 0 || first % vk::PLACE_WINDOW != 0 || first + count > ix->n_pad)

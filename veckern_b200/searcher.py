@@ -245,6 +245,70 @@ class PQSearcher:
         return out
 
 
+class MultiPQSearcher:
+    """One database split into contiguous row shards over several GPUs of this process (vk_multi_*): every shard
+    searches on its own device and stream, the per-shard lists are gathered and merged on devices[0]. Results are
+    identical to one PQSearcher over all rows."""
+
+    def __init__(self, centroids, codes=None, *, devices=(0,), _handle=None):
+        self._h = C.c_void_p()
+        self.tuning = Tuning()
+        if _handle is not None:
+            self._h = _handle
+        else:
+            centroids = np.ascontiguousarray(centroids, np.float32)
+            codes = np.ascontiguousarray(codes, np.uint8)
+            m, _, dsub = centroids.shape
+            if codes.ndim != 2 or codes.shape[1] != m:
+                raise ValueError("codes must be [n, m] uint8")
+            devs = np.ascontiguousarray(devices, np.int32)
+            check(lib().vk_multi_create(len(devs), ptr(devs), ptr(centroids), m, dsub, ptr(codes), codes.shape[0],
+                                        C.byref(self._h)), "vk_multi_create")
+        n, shards = C.c_int64(), C.c_int()
+        check(lib().vk_multi_info(self._h, C.byref(n), C.byref(shards)))
+        self.n, self.shards = n.value, shards.value
+
+    @classmethod
+    def load(cls, path: str, *, devices=(0,), verify: bool = True) -> "MultiPQSearcher":
+        devs = np.ascontiguousarray(devices, np.int32)
+        h = C.c_void_p()
+        check(lib().vk_multi_load(len(devs), ptr(devs), str(path).encode(), int(verify), C.byref(h)), "vk_multi_load")
+        return cls(None, _handle=h)
+
+    def set_tuning(self, tuning: Tuning) -> None:
+        t = tuning.c()
+        check(lib().vk_tuning_validate(C.byref(t)), "set_tuning")
+        self.tuning = tuning
+
+    def search(self, queries, k: int, out: np.ndarray | None = None):
+        """HOST queries [nq, d] -> HOST results [nq, k] (NEIGHBOR_DTYPE), Timings."""
+        queries = np.ascontiguousarray(queries, np.float32)
+        queries = queries.reshape(-1, queries.shape[-1]) if queries.ndim > 1 else queries.reshape(1, -1)
+        nq = queries.shape[0]
+        if out is None:
+            out = empty_neighbors(nq, k)
+        t, tun = N.Timings(), self.tuning.c()
+        check(lib().vk_multi_search(self._h, ptr(queries), nq, k, C.byref(tun), ptr(out), C.byref(t)), "multi search")
+        return out, Timings(t.transfer_ms, t.lut_ms, t.scan_ms, t.select_ms)
+
+    def close(self) -> None:
+        if self._h:
+            lib().vk_multi_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
 def _stream_handle(stream):
     """cudaStream_t of a torch.cuda.Stream / raw handle; None -> torch's current stream (0 = default stream)."""
     if stream is None:
