@@ -373,6 +373,10 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                         for (int q = 0; q < Q; ++q) top[q].offer(acc[u][q], ids[u], valid[u], a.k);
                 }
             } else {
+                // The query group's global bounds, loaded now (lane q: query q) so that the L2 latency hides
+                // behind phase A; other warps and blocks keep lowering them.
+                float gb = __int_as_float(0x7f800000);
+                if (lane < Q && (int64_t)g * Q + lane < a.nq) gb = __uint_as_float(__ldcg(a.bound + (int64_t)g * Q + lane));
                 // ---- phase A: sub-spaces [0, SA) of every row, all Q queries per fetch
                 float acc[ILP][Q];
 #pragma unroll
@@ -393,8 +397,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                 float bnd[Q];
 #pragma unroll
                 for (int q = 0; q < Q; ++q) {
-                    const int64_t qi = (int64_t)g * Q + q;
-                    if (qi < a.nq) known[q] = fminf(known[q], __uint_as_float(__ldcg(a.bound + qi)));
+                    known[q] = fminf(known[q], __shfl_sync(FULL, gb, q));  // padded slots keep -1
                     bnd[q] = fminf(known[q], top[q].thr_d);
                 }
                 // ---- surviving (row, query) pairs
@@ -450,10 +453,12 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                     for (int u = 0; u < ILP; ++u)
 #pragma unroll
                         for (int q = 0; q < Q; ++q) {
-                            if ((masks[u][q] >> lane) & 1u)
-                                my_queue[cnt + __popc(masks[u][q] & lt)] =
-                                    make_int2(__float_as_int(acc[u][q]), (u * 32 + lane) | (q << 16));
-                            cnt += __popc(masks[u][q]);
+                            if (masks[u][q] != 0) {  // uniform: most (row group, query) ballots are empty
+                                if ((masks[u][q] >> lane) & 1u)
+                                    my_queue[cnt + __popc(masks[u][q] & lt)] =
+                                        make_int2(__float_as_int(acc[u][q]), (u * 32 + lane) | (q << 16));
+                                cnt += __popc(masks[u][q]);
+                            }
                         }
                 }
                 __syncwarp();
