@@ -266,6 +266,17 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def finite(x):
+    """NaN / inf (e.g. full-scan figures under --skip-full) become null, so the line is strict JSON."""
+    if isinstance(x, dict):
+        return {k: finite(v) for k, v in x.items()}
+    if isinstance(x, list):
+        return [finite(v) for v in x]
+    if isinstance(x, float) and not np.isfinite(x):
+        return None
+    return x
+
+
 def workload_name(s, cfg):
     return f"{cfg}: flat PQ search n={s['n']:,} d={s['d']} m={s['m']} nq={s['nq']:,} k={s['k']}"
 
@@ -428,13 +439,18 @@ def run_ours(args):
         smem_peak_bytes = 128.0 * info.sm_count * sm_mhz * 1e6
         Q = s.last_launch().queries_per_block
         wf = wf_rows = None
+        sample = 1 << 17
         if w.codes is not None:
-            # the device layout: rows of whole 64-row windows in the index's lane placement
-            perm = s.get_placement()
-            full = w.codes.shape[0] // 64 * 64
-            placed = np.concatenate([w.codes[(np.arange(full) & ~63) + perm[:full]], w.codes[full:]])
-            wf = lookup_wavefront_model(placed, Q)
-            wf_rows = lookup_wavefront_model(w.codes, Q)
+            rows_codes = w.codes[:sample]
+        else:  # generated configs: the shard's first rows, regenerated on the host
+            from veckern_b200 import data as vkdata
+            rows_codes = vkdata.gen_codes(spec["code_seed"], w.cdf, lo, min(sample, hi - lo))
+        # the device layout: rows of whole 64-row windows in the index's lane placement
+        perm = s.get_placement(rows_codes.shape[0])
+        full = rows_codes.shape[0] // 64 * 64
+        placed = np.concatenate([rows_codes[(np.arange(full) & ~63) + perm[:full]], rows_codes[full:]])
+        wf = lookup_wavefront_model(placed, Q)
+        wf_rows = lookup_wavefront_model(rows_codes, Q)
         per_fetch = 4 if Q >= 4 else Q  # lookups served per warp LUT fetch per lane
         fetches = lookups / 32.0 / per_fetch
         floor_ms = fetches * wf / (info.sm_count * sm_mhz * 1e6) * 1e3 if wf else None
@@ -479,7 +495,7 @@ def run_ours(args):
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
             "verified_against_single_gpu": verified,
         }
-        print(json.dumps(line), flush=True)
+        print(json.dumps(finite(line)), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

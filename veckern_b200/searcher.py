@@ -237,11 +237,13 @@ class PQSearcher:
         check(lib().vk_index_get_codes(self._h, first, count, ptr(out)), "get_codes")
         return out
 
-    def get_placement(self) -> np.ndarray:
-        """[n_pad] uint8: row (within its 64-position window) stored at each position of the device layout."""
+    def get_placement(self, count: int | None = None) -> np.ndarray:
+        """uint8 per position of the device layout (the first `count`, default all n_pad): the row, within its
+        64-position window, stored there."""
         n_pad = (self.n + 127) // 128 * 128
-        out = np.empty(n_pad, np.uint8)
-        check(lib().vk_index_get_placement(self._h, 0, n_pad, ptr(out)), "get_placement")
+        count = n_pad if count is None else min(n_pad, count)
+        out = np.empty(count, np.uint8)
+        check(lib().vk_index_get_placement(self._h, 0, count, ptr(out)), "get_placement")
         return out
 
 
