@@ -545,11 +545,13 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
         auto merge_and_publish = [&](int64_t qi, const int2* slot_lists, float kb) {
             WarpTopK<S> mt;
             mt.init();
+            // Pairs above kb (an upper bound of the query's final k-th distance) cannot be in the result, so they
+            // are left out of the item's list: fewer insertions, same final merge.
             const int total = NW * a.k;
             for (int j0 = 0; j0 < total; j0 += 32) {
                 const int j = j0 + lane;
                 const int2 e = j < total ? slot_lists[j] : make_int2(0x7f800000, SENTINEL_ID);
-                mt.offer(__int_as_float(e.x), e.y, j < total, a.k);
+                mt.offer(__int_as_float(e.x), e.y, j < total && !(__int_as_float(e.x) > kb), a.k);
             }
             mt.store(a.part + (qi * a.chunks + chunk) * a.k, a.k);  // this item's own list
             if constexpr (PRUNE) {
