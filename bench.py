@@ -52,6 +52,9 @@ def parse():
     p.add_argument("--skip-full", action="store_true", help="skip the full-scan (early_abandon=0) comparison loops")
     p.add_argument("--verify", action="store_true",
                    help="rank 0 also searches the whole database on its GPU and checks the merged result bit-exactly")
+    p.add_argument("--rerank", type=int, default=0,
+                   help="one GPU: each step is the PQ search for k candidates followed by the exact re-rank of them to "
+                        "this many neighbours (the reference's --rerank); reports recall@R with and without it")
     return p.parse_args()
 
 
@@ -549,10 +552,84 @@ def cpu_baseline(args, w, spec):
             "sample": f"{sample} of {spec['nq']} queries over the full {spec['n']:,}-row database ({dt:.1f} s)"}
 
 
+def exact_topk(base, queries, k, chunk=1 << 20):
+    """Ground truth for recall: exact squared L2 in float64 on the GPU (torch), k smallest ids per query."""
+    import torch
+    q = queries.double()
+    qn = (q * q).sum(1, keepdim=True)
+    best_d = torch.full((q.shape[0], k), float("inf"), dtype=torch.float64, device=q.device)
+    best_i = torch.full((q.shape[0], k), -1, dtype=torch.int64, device=q.device)
+    for a in range(0, base.shape[0], chunk):
+        xb = base[a:a + chunk].double()
+        dist = qn - 2.0 * q @ xb.T + (xb * xb).sum(1)[None, :]
+        d2 = torch.cat([best_d, dist], 1)
+        i2 = torch.cat([best_i, torch.arange(a, a + xb.shape[0], device=q.device).expand(q.shape[0], -1)], 1)
+        best_d, idx = torch.topk(d2, k, dim=1, largest=False)
+        best_i = torch.gather(i2, 1, idx)
+    return best_i.cpu().numpy()
+
+
+def run_rerank(args):
+    """PQ search for spec k candidates + exact GPU re-rank to args.rerank neighbours, on one GPU (config 2 is the
+    reference's re-ranking candidate pass, bench_main.cpp:146-153)."""
+    import torch
+
+    from veckern_b200 import PQSearcher, Tuning, device_result_split, rerank_device
+    from veckern_b200 import configs
+
+    torch.cuda.set_device(0)
+    spec = configs.spec(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k)
+    w = configs.make(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k, keep_base=True, encode=gpu_encoder(),
+                     train=gpu_trainer())
+    nq, r, k = spec["nq"], spec["k"], args.rerank
+    s = PQSearcher(w.centroids, w.codes, device=0)
+    s.set_tuning(Tuning(queries_per_block=args.qpb, vectors_per_step=args.ilp))
+    d_base = torch.from_numpy(w.base).cuda()
+    d_q = torch.from_numpy(w.queries).cuda()
+    d_cand = torch.empty((nq, r), dtype=torch.int64, device="cuda")
+    d_out = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step():
+        s.search_device(d_q, r, d_cand, stream)
+        rerank_device(0, d_base, d_q, d_cand, k, d_out, stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    s.sync(stream)
+    ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    sample = min(nq, 100)
+    truth = exact_topk(d_base, d_q[:sample], k)
+    pq_ids = device_result_split(d_cand)[1][:sample, :k].cpu().numpy()
+    rr_ids = device_result_split(d_out)[1][:sample].cpu().numpy()
+    recall = lambda ids: float(np.mean([len(set(a) & set(b)) / k for a, b in zip(ids, truth)]))  # noqa: E731
+    line = {"metric": "queries/s", "value": round(nq / (ms / 1e3), 1), "unit": "queries/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": workload_name(spec, args.config) + f" + exact re-rank of {r} candidates to {k}",
+                       "l2": "flushed (256 MB write) before every timed step"},
+            "recall_at_k": {"k": k, "queries": sample, "pq_only": round(recall(pq_ids), 4),
+                            "with_rerank": round(recall(rr_ids), 4),
+                            "truth": "exact squared L2 in float64 over all rows"}}
+    print(json.dumps(finite(line)), flush=True)
+    s.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.rerank:
+        run_rerank(args)
     else:
         run_ours(args)
 
