@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstring>
 #include <limits>
+#include <map>
 #include <mutex>
 #include <numeric>
 #include <random>
@@ -159,6 +160,10 @@ struct vk_index {
     cudaEvent_t ev[6] = {};
     int sm_count = 0, smem_optin = 0, clock_khz = 0;
     long long wait_budget = 0;
+    // Launch set-up already done on this device: dynamic shared memory granted per kernel, and resident blocks per
+    // SM per (kernel, shared memory, threads); saves two driver calls per search.
+    mutable std::map<const void*, uint32_t> smem_granted;
+    mutable std::map<std::pair<const void*, uint64_t>, int> resident_per_sm;
 
     ~vk_index() {
         DeviceGuard g(device);
@@ -221,9 +226,20 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     if (!p.fn) return fail(VK_ERR_UNSUPPORTED, "no scan kernel for Q=%d m=%d ilp=%d", Q, ix->m, p.ilp);
     p.merge_slots = slots(Q);
     p.smem = vk::scan_smem_plan(Q, ix->m, ix->W, p.ilp, nw, p.stages, k, p.prune, p.merge_slots).total;
-    VK_TRY_CUDA(cudaFuncSetAttribute(p.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+    auto granted = ix->smem_granted.find(p.fn);
+    if (granted == ix->smem_granted.end() || granted->second < p.smem) {
+        VK_TRY_CUDA(cudaFuncSetAttribute(p.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+        ix->smem_granted[p.fn] = p.smem;
+    }
+    const auto occ_key = std::make_pair(p.fn, ((uint64_t)p.smem << 16) | (uint64_t)p.threads);
+    auto occ = ix->resident_per_sm.find(occ_key);
     int per_sm = 0;
-    VK_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, p.fn, p.threads, p.smem));
+    if (occ != ix->resident_per_sm.end()) {
+        per_sm = occ->second;
+    } else {
+        VK_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, p.fn, p.threads, p.smem));
+        ix->resident_per_sm[occ_key] = per_sm;
+    }
     p.blocks_per_sm = std::max(per_sm, 1);
     const int64_t resident = (int64_t)p.blocks_per_sm * ix->sm_count;
 
