@@ -643,4 +643,49 @@ __global__ void __launch_bounds__(128) merge_kernel(const int2* __restrict__ in,
     }
 }
 
+// Few queries (the latency case): one block of 8 warps per query. Warp w keeps the k best of candidates
+// w * 32 + lane, w * 32 + 256 + lane, ...; warp 0 then merges the 8 lists. The k smallest of distinct (dist, id)
+// pairs do not depend on the merge order, so the result equals merge_kernel's.
+template <int S>
+__global__ void __launch_bounds__(256) merge_wide_kernel(const int2* __restrict__ in, int64_t nq, int lists, int k_in,
+                                                         int64_t qstride, int64_t lstride, int k,
+                                                         int2* __restrict__ out) {
+    constexpr int NWM = 8;
+    __shared__ int2 part[NWM * 32 * S];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t q = blockIdx.x;
+    if (q >= nq) return;  // block-uniform
+    const int2* base = in + q * qstride;
+    const int64_t total = (int64_t)lists * k_in;
+    WarpTopK<S> top;
+    top.init();
+    for (int64_t j0 = (int64_t)warp * 32; j0 < total; j0 += NWM * 32) {
+        const int64_t j = j0 + lane;
+        int2 e = make_int2(0x7f800000, SENTINEL_ID);
+        if (j < total) {
+            const int64_t l = j / k_in, i = j - l * k_in;
+            e = base[l * lstride + i];
+        }
+        top.offer(__int_as_float(e.x), e.y, j < total && e.y >= 0, k);
+    }
+    top.store(part + warp * k, k);
+    __syncthreads();
+    if (warp != 0) return;
+    WarpTopK<S> fin;
+    fin.init();
+    for (int j0 = 0; j0 < NWM * k; j0 += 32) {
+        const int j = j0 + lane;
+        const int2 e = j < NWM * k ? part[j] : make_int2(0x7f800000, SENTINEL_ID);
+        fin.offer(__int_as_float(e.x), e.y, j < NWM * k, k);
+    }
+#pragma unroll
+    for (int r = 0; r < S; ++r) {
+        const int e = r * 32 + lane;
+        if (e < k) {
+            const bool pad = fin.id[r] == SENTINEL_ID;
+            out[q * k + e] = pad ? make_int2(0x7f800000, -1) : make_int2(__float_as_int(fin.d[r]), fin.id[r]);
+        }
+    }
+}
+
 }  // namespace vk

@@ -138,6 +138,14 @@ const void* merge_kernel_ptr(int s) {
     }
 }
 
+const void* merge_wide_kernel_ptr(int s) {
+    switch (s) {
+        case 1: return reinterpret_cast<const void*>(&vk::merge_wide_kernel<1>);
+        case 2: return reinterpret_cast<const void*>(&vk::merge_wide_kernel<2>);
+        default: return reinterpret_cast<const void*>(&vk::merge_wide_kernel<4>);
+    }
+}
+
 int s_for_k(int k) { return k <= 32 ? 1 : k <= 64 ? 2 : 4; }
 
 }  // namespace
@@ -367,15 +375,20 @@ int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk
         VK_TRY_CUDA(cudaLaunchKernel(p.fn, dim3(p.grid), dim3(p.threads), args, p.smem, st));
     }
     if (marks) VK_TRY_CUDA(cudaEventRecord(marks[1], st));
-    // merge of the per-chunk partial lists
+    // merge of the per-chunk partial lists: one warp per query, or, when there are fewer queries than SMs and many
+    // lists, one 8-warp block per query
     {
-        const void* fn = merge_kernel_ptr(p.S);
+        const bool wide = nq <= ix->sm_count && (int64_t)p.chunks * k >= 256;
+        const void* fn = wide ? merge_wide_kernel_ptr(p.S) : merge_kernel_ptr(p.S);
         const int2* in = ix->part.ptr;
         int lists = p.chunks, k_in = k, kk = k;
         int64_t qstride = (int64_t)p.chunks * k, lstride = k;
         void* args[] = {(void*)&in, (void*)&nq, (void*)&lists, (void*)&k_in, (void*)&qstride, (void*)&lstride,
                         (void*)&kk, (void*)&d_out};
-        VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)ceil_div(nq, 4)), dim3(128), args, 0, st));
+        if (wide)
+            VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)nq), dim3(256), args, 0, st));
+        else
+            VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)ceil_div(nq, 4)), dim3(128), args, 0, st));
     }
     if (shape) {
         shape->threads = p.threads;
