@@ -279,17 +279,25 @@ __global__ void __launch_bounds__(256) train_sums_kernel(const float* __restrict
     if (c >= KSUB) return;  // warp-uniform
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     int count = 0;
-    for (int64_t i0 = 0; i0 < n; i0 += 32) {
-        const int64_t i = i0 + lane;
-        unsigned mask = __ballot_sync(FULL, i < n && assign[i] == c);
-        count += __popc(mask);
-        while (mask) {
-            const int64_t row = i0 + __ffs(mask) - 1;
-            mask &= mask - 1;
-            const float* v = x + row * d + (int64_t)s * dsub;
+    for (int64_t i0 = 0; i0 < n; i0 += 128) {  // four 32-row groups per step: their loads are in flight together
+        int a[4];
 #pragma unroll
-            for (int r = 0; r < 4; ++r)
-                if (lane + 32 * r < dsub) acc[r] = __fadd_rn(acc[r], v[lane + 32 * r]);
+        for (int g = 0; g < 4; ++g) {
+            const int64_t i = i0 + 32 * g + lane;
+            a[g] = i < n ? assign[i] : -1;
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {  // groups in row order, rows within a group in order
+            unsigned mask = __ballot_sync(FULL, a[g] == c);
+            count += __popc(mask);
+            while (mask) {
+                const int64_t row = i0 + 32 * g + __ffs(mask) - 1;
+                mask &= mask - 1;
+                const float* v = x + row * d + (int64_t)s * dsub;
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+                    if (lane + 32 * r < dsub) acc[r] = __fadd_rn(acc[r], v[lane + 32 * r]);
+            }
         }
     }
 #pragma unroll
@@ -336,6 +344,67 @@ __global__ void __launch_bounds__(256) encode_kernel(const float* __restrict__ c
         }
     }
     codes[i * m + s] = (uint8_t)best;
+}
+
+// Shape-specialised versions of encode_kernel / train_assign_kernel for dsub in {1, 2, 4, 8, 16, 32}: the row's
+// sub-vector in registers, four centroids' distances computed side by side (each summed over j in order, every
+// operation rounded on its own), then compared in centroid order, so the first minimum still wins.
+template <int DSUB>
+__device__ __forceinline__ int nearest_centroid(const float (&v)[DSUB], const float* __restrict__ cen) {
+    int best = 0;
+    float best_d = FLT_MAX;
+    for (int c = 0; c < KSUB; c += 4) {
+        float acc[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            acc[t] = 0.f;
+#pragma unroll
+            for (int j = 0; j < DSUB; ++j) {
+                const float diff = __fsub_rn(v[j], cen[(c + t) * DSUB + j]);
+                acc[t] = __fadd_rn(acc[t], __fmul_rn(diff, diff));
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            if (acc[t] < best_d) {
+                best_d = acc[t];
+                best = c + t;
+            }
+        }
+    }
+    return best;
+}
+
+template <int DSUB>
+__global__ void __launch_bounds__(256) encode_kernel_t(const float* __restrict__ centroids, int m,
+                                                       const float* __restrict__ x, int64_t n,
+                                                       uint8_t* __restrict__ codes) {
+    __shared__ float scen[KSUB * DSUB];
+    const int s = blockIdx.y;
+    for (int t = threadIdx.x; t < KSUB * DSUB; t += blockDim.x) scen[t] = centroids[(int64_t)s * KSUB * DSUB + t];
+    __syncthreads();
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float* xs = x + i * ((int64_t)m * DSUB) + (int64_t)s * DSUB;
+    float v[DSUB];
+#pragma unroll
+    for (int j = 0; j < DSUB; ++j) v[j] = xs[j];
+    codes[i * m + s] = (uint8_t)nearest_centroid<DSUB>(v, scen);
+}
+
+template <int DSUB>
+__global__ void __launch_bounds__(256) train_assign_kernel_t(const float* __restrict__ x, int64_t n, int d, int s,
+                                                             const float* __restrict__ cent, int* __restrict__ assign) {
+    __shared__ float tcen[KSUB * DSUB];
+    for (int t = threadIdx.x; t < KSUB * DSUB; t += blockDim.x) tcen[t] = cent[t];
+    __syncthreads();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float* xs = x + i * d + (int64_t)s * DSUB;
+        float v[DSUB];
+#pragma unroll
+        for (int j = 0; j < DSUB; ++j) v[j] = xs[j];
+        assign[i] = nearest_centroid<DSUB>(v, tcen);
+    }
 }
 
 // ------------------------------------------------------------------------------------------------ re-rank

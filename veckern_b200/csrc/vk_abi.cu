@@ -1186,7 +1186,16 @@ int vk_encode_device(int device, const float* centroids, int m, int dsub, const 
     if (smem > 48 * 1024)
         VK_TRY_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(&vk::encode_kernel),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    vk::encode_kernel<<<dim3((unsigned)ceil_div(n, 256), m), 256, smem, st>>>(d_cen, m, dsub, d_x, n, d_codes);
+    const dim3 egrid((unsigned)ceil_div(n, 256), m);
+    switch (dsub) {
+        case 1: vk::encode_kernel_t<1><<<egrid, 256, 0, st>>>(d_cen, m, d_x, n, d_codes); break;
+        case 2: vk::encode_kernel_t<2><<<egrid, 256, 0, st>>>(d_cen, m, d_x, n, d_codes); break;
+        case 4: vk::encode_kernel_t<4><<<egrid, 256, 0, st>>>(d_cen, m, d_x, n, d_codes); break;
+        case 8: vk::encode_kernel_t<8><<<egrid, 256, 0, st>>>(d_cen, m, d_x, n, d_codes); break;
+        case 16: vk::encode_kernel_t<16><<<egrid, 256, 0, st>>>(d_cen, m, d_x, n, d_codes); break;
+        case 32: vk::encode_kernel_t<32><<<egrid, 256, 0, st>>>(d_cen, m, d_x, n, d_codes); break;
+        default: vk::encode_kernel<<<egrid, 256, smem, st>>>(d_cen, m, dsub, d_x, n, d_codes); break;
+    }
     VK_TRY_CUDA(cudaGetLastError());
     VK_TRY_CUDA(cudaFreeAsync(d_cen, st));
     return VK_OK;
@@ -1230,7 +1239,17 @@ int vk_pq_train_device(int device, const float* d_x, int64_t n, int d, int m, in
         vk::train_gather_kernel<<<1, 256, 0, st>>>(d_x, d, s, dsub, rows.ptr, cent.ptr);
         VK_TRY_CUDA(cudaGetLastError());
         for (int64_t it = 0; it < iters; ++it) {
-            vk::train_assign_kernel<<<agrid, 256, cbytes, st>>>(d_x, n, d, s, dsub, cent.ptr, assign.ptr);
+            switch (dsub) {
+                case 1: vk::train_assign_kernel_t<1><<<agrid, 256, 0, st>>>(d_x, n, d, s, cent.ptr, assign.ptr); break;
+                case 2: vk::train_assign_kernel_t<2><<<agrid, 256, 0, st>>>(d_x, n, d, s, cent.ptr, assign.ptr); break;
+                case 4: vk::train_assign_kernel_t<4><<<agrid, 256, 0, st>>>(d_x, n, d, s, cent.ptr, assign.ptr); break;
+                case 8: vk::train_assign_kernel_t<8><<<agrid, 256, 0, st>>>(d_x, n, d, s, cent.ptr, assign.ptr); break;
+                case 16: vk::train_assign_kernel_t<16><<<agrid, 256, 0, st>>>(d_x, n, d, s, cent.ptr, assign.ptr); break;
+                case 32: vk::train_assign_kernel_t<32><<<agrid, 256, 0, st>>>(d_x, n, d, s, cent.ptr, assign.ptr); break;
+                default:
+                    vk::train_assign_kernel<<<agrid, 256, cbytes, st>>>(d_x, n, d, s, dsub, cent.ptr, assign.ptr);
+                    break;
+            }
             VK_TRY_CUDA(cudaGetLastError());
             vk::train_sums_kernel<<<vk::KSUB / 8, 256, 0, st>>>(d_x, n, d, s, dsub, assign.ptr, sums.ptr, counts.ptr);
             VK_TRY_CUDA(cudaGetLastError());
