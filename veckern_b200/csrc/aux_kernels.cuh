@@ -79,8 +79,9 @@ __global__ void deinterleave_kernel(const uint4* __restrict__ codes, const uint8
 // table lies in group c mod P. The cost of a placement is the sum over sub-spaces (weight w_s) and phases of the
 // largest number of the phase's rows whose codes share a group, i.e. the fetch's wavefronts when no two of those
 // rows hold the same code. Hill climbing: `steps` swaps of two positions in different phases, drawn from a
-// per-window counter-based sequence (deterministic layout), each kept when it does not raise the cost. Weights
-// follow the pruned scan: w = 20 for s < first_depth (phase A of every row), 6 for s < last_depth, 1 beyond.
+// per-window xorshift sequence seeded by a counter-based hash (deterministic layout), each kept when it does not
+// raise the cost. Weights follow the pruned scan: w = 20 for s < first_depth (phase A of every row), 6 for
+// s < last_depth, 1 beyond.
 // One warp per window; lane l keeps the counts of sub-spaces l and l + 32.
 __host__ __device__ constexpr uint32_t place_warp_smem(int m, int W) { return (uint32_t)(PLACE_WINDOW * W * 16 + PLACE_WINDOW * m + PLACE_WINDOW); }
 
@@ -132,9 +133,12 @@ __global__ void __launch_bounds__(128) place_rows_kernel(uint4* __restrict__ cod
                     ++cnt[((p / P) * m + s) * P + (row_codes[p * W * 16 + s] & (P - 1))];
         }
         __syncwarp();
+        uint32_t rs = (uint32_t)mix64(key ^ (uint64_t)win) | 1u;  // xorshift32 state, seeded per window
         for (int it = 0; it < steps; ++it) {
-            const uint64_t hsh = mix64(key ^ mix64((uint64_t)win * 0x100000000ull + (uint64_t)it));
-            const int i = (int)(hsh & 63), j = (int)((hsh >> 6) & 63);
+            rs ^= rs << 13;
+            rs ^= rs >> 17;
+            rs ^= rs << 5;
+            const int i = (int)(rs & 63u), j = (int)((rs >> 6) & 63u);
             const int pa = i / P, pb = j / P;
             if (pa == pb) continue;  // uniform: every lane draws the same pair
             const int ri = order[i], rj = order[j];
