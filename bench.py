@@ -50,8 +50,14 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample duration")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--skip-full", action="store_true", help="skip the full-scan (early_abandon=0) comparison loops")
-    p.add_argument("--verify", action="store_true",
-                   help="rank 0 also searches the whole database on its GPU and checks the merged result bit-exactly")
+    p.add_argument("--no-verify", action="store_true",
+                   help="N > 1: skip rank 0's search of the whole database on its GPU, which checks the merged results "
+                        "bit-exactly (done by default)")
+    p.add_argument("--sharded", default="c3",
+                   help="generated configuration (c3 or c4) also measured sharded by id over the run's GPUs, reported "
+                        "under 'sharded'; 'none' to skip")
+    p.add_argument("--sharded-steps", type=int, default=2)
+    p.add_argument("--sharded-warmup", type=int, default=3)
     p.add_argument("--rerank", type=int, default=0,
                    help="one GPU: each step is the PQ search for k candidates followed by the exact re-rank of them to "
                         "this many neighbours (the reference's --rerank); reports recall@R with and without it")
@@ -161,15 +167,26 @@ class ClockSampler:
                 "power_w_max": round(max(r[2] for r in rows), 1)}
 
 
-# DRAM bytes per launch of the default scan kernel from the ncu capture summarised in profiles/ (same bench command,
-# one GPU); reported only for the workload it was captured on.
-NCU_TRAFFIC = {("c1", 1_000_000, 16, 1000, 10): {"dram_bytes_per_launch": 33_660_416,
-                                                 "source": "profiles/scan_kernel_c1_m16.md (ncu, dram__bytes_read.sum "
-                                                           "+ dram__bytes_write.sum)"}}
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the default scan kernel, from ncu
+# captures of these workloads on one B200 (the capture commands and their other counters are in profiles/). Keyed by
+# (config, rows scanned per GPU, m, nq, k); a run whose shard matches no capture reports the bytes scaled from the
+# capture of the same config by rows (codes and placement bytes grow with rows, LUT bytes with nq), marked scaled.
+NCU_TRAFFIC = {
+    ("c1", 1_000_000, 16, 1000, 10): {"dram_bytes_per_launch": 33_660_416, "kernel": "scan_kernel<8,16,2,1,16,1>"},
+}
 
 
-def ncu_traffic(config, spec, world):
-    return NCU_TRAFFIC.get((config, spec["n"], spec["m"], spec["nq"], spec["k"])) if world == 1 else None
+def ncu_traffic(config, rows, m, nq, k):
+    hit = NCU_TRAFFIC.get((config, rows, m, nq, k))
+    if hit:
+        return dict(hit, captured=True)
+    for (c, r, mm, q, kk), v in NCU_TRAFFIC.items():
+        if c == config and mm == m and q == nq and kk == k:
+            lut = nq * m * 256 * 4
+            per_row = (v["dram_bytes_per_launch"] - lut) / r
+            return {"dram_bytes_per_launch": int(lut + per_row * rows), "kernel": v["kernel"], "captured": False,
+                    "scaled_from_rows": r}
+    return None
 
 
 def lookup_wavefront_model(codes: np.ndarray, Q: int, sample_rows: int = 1 << 17) -> float:
@@ -223,50 +240,135 @@ def gpu_trainer():
 
 
 # ------------------------------------------------------------------------------------------------ reference arm
+def usable_cores() -> int:
+    """Host threads this process may run on (its CPU affinity), the reference CPU path's thread count."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def run_reference(args):
+    """The reference's own CPU search (adc_search, oracle/_ref) with every usable host thread, on a bounded query
+    sample per step. The workload is built without this repository's libraries: inputs by the numpy restatement of
+    the configuration's generators (oracle/inputs.py), codebook and codes by the reference's own ProductQuantizer.
+    At N = 1 it also runs the reference's own GPU kernel (v8, FusedWarp, compiled for sm_100a from its sources) on
+    the same inputs over its tuning sweep (key reference_gpu_v8)."""
     rank, world, _ = rank_info()
     if rank != 0:
         return
+    cores = usable_cores()
+    # torchrun exports OMP_NUM_THREADS=1; libgomp reads the variable when it loads, which happens below
+    os.environ["OMP_NUM_THREADS"] = str(cores)
     import oracle
-    from veckern_b200 import configs
+    from veckern_b200.configs import spec as config_spec  # a plain dict: loads no library
 
+    s = config_spec(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k)
     kind = "reference" if oracle.ref_available() else "port"
-    w = configs.make(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k)
-    s = w.spec
-    cores = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
-    if kind == "reference":
+    t_setup = time.perf_counter()
+    pq = None
+    if kind == "reference" and s["kind"] in ("normal", "mixture"):
+        from oracle import inputs
         R = oracle.ref()
-        pq = R.pq(s["d"], s["m"])
-        pq.centroids = w.centroids
-        run = lambda q: R.adc_search(pq, w.codes, q, s["k"])  # noqa: E731
+        threads = R.set_threads(cores)
+        pq, codes, queries = inputs.reference_workload(s, R)
+        centroids = pq.centroids
+        inputs_by = "numpy generators (oracle/inputs.py) + the reference's ProductQuantizer train/encode"
+        run = lambda q: R.adc_search(pq, codes, q, s["k"])  # noqa: E731
     else:
-        P = oracle.port()
-        run = lambda q: P.adc_search(w.centroids, w.codes, q, s["k"], cores)  # noqa: E731
+        from veckern_b200 import configs
+        w = configs.make(args.config, n=args.n, m=args.m, nq=args.nq, k=args.k)
+        if w.codes is None:
+            from veckern_b200 import data
+            w.codes = data.gen_codes(s["code_seed"], w.cdf, 0, s["n"])
+        centroids, codes, queries = w.centroids, w.codes, w.queries
+        inputs_by = "the package's host generators"
+        if kind == "reference":
+            R = oracle.ref()
+            threads = R.set_threads(cores)
+            pq = R.pq(s["d"], s["m"])
+            pq.centroids = centroids
+            run = lambda q: R.adc_search(pq, codes, q, s["k"])  # noqa: E731
+        else:
+            P = oracle.port()
+            threads = cores
+            run = lambda q: P.adc_search(centroids, codes, q, s["k"], cores)  # noqa: E731
+    setup_s = time.perf_counter() - t_setup
+    nq = s["nq"]
+    probe_n = max(1, min(cores, nq))
     t0 = time.perf_counter()
-    run(w.queries[:max(1, min(8, s["nq"]))])
-    probe = time.perf_counter() - t0
-    per_q = probe / max(1, min(8, s["nq"]))
+    run(queries[:probe_n])
+    per_q = (time.perf_counter() - t0) / probe_n
     per_step = 60.0 / max(1, args.steps + args.warmup)  # the whole reference run stays near one minute
-    sample = int(max(1, min(s["nq"], per_step / max(per_q, 1e-9))))
+    sample = int(max(1, min(nq, per_step / max(per_q, 1e-9))))
     for i in range(args.warmup):
-        run(w.queries[:sample])
-    times = []
+        run(queries[:sample])
+    times, counts = [], []
+    cpu_res = None
     for i in range(args.steps):
+        q0 = (i * sample) % nq
+        qs = queries[q0:q0 + sample]
         t0 = time.perf_counter()
-        run(w.queries[(i * sample) % s["nq"]:][:sample])
+        res = run(qs)
         times.append(time.perf_counter() - t0)
-    qps = sample / float(np.mean(times))
+        counts.append(qs.shape[0])
+        if i == 0:
+            cpu_res = (q0, res)
+    qps = float(np.sum(counts)) / float(np.sum(times)) if times else 0.0
     line = {"impl": "reference", "metric": "queries/s", "value": round(qps, 3), "unit": "queries/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(1e3 * float(np.mean(times)), 3), "higher_is_better": True,
+            "ms_per_step": round(1e3 * float(np.mean(times)), 3) if times else None, "higher_is_better": True,
             "config": {"workload": workload_name(s, args.config), "n": s["n"], "m": s["m"], "nq_sample": sample,
                        "k": s["k"]},
             "dtype": "f32", "data": "synthetic",
-            "cpu_baseline": {"value": round(qps, 3), "unit": "queries/s", "cores": cores, "kind": kind,
-                             "sample": f"{sample} of {s['nq']} queries per step, full database of {s['n']} rows"},
+            "cpu_baseline": {"value": round(qps, 3), "unit": "queries/s", "cores": threads, "kind": kind,
+                             "sample": f"{sample} of {nq} queries per step, full database of {s['n']} rows",
+                             "inputs": inputs_by, "setup_s": round(setup_s, 1)},
             "e2e": {"value": round(qps, 3), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    if world == 1 and pq is not None:
+        line["reference_gpu_v8"] = reference_gpu_v8(centroids, codes, queries, s, cpu_res)
+    print(json.dumps(finite(line)), flush=True)
+
+
+def reference_gpu_v8(centroids, codes, queries, s, cpu_res):
+    """The reference's final kernel (FusedWarp through its own PQSearcher, searcher.cu compiled for sm_100a) on the
+    same inputs: its default tuning and the best point of its own queries_per_block x ilp sweep
+    (scripts/run_all.sh:87-91), each the median of 5 searches after a warm-up (bench/bench_main.cpp:191-214).
+    q/s = nq / (transfer + lut + scan + select), the reference's own definition. ids_equal_cpu: share of the
+    (query, rank) ids equal to the reference CPU path on the timed CPU sample (its v8 regroups additions)."""
+    import oracle
+    if not oracle.refgpu_available():
+        return {"unavailable": "oracle/_ref/libveckern_refgpu.so not built (needs the reference sources)"}
+    if s["m"] % 16 != 0:
+        return {"unavailable": "the reference's v8 requires m % 16 == 0"}
+    try:
+        import torch
+        if not torch.cuda.is_available():
+            return {"unavailable": "no GPU"}
+        name = torch.cuda.get_device_name(0)
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"torch: {e}"}
+    points = [(2, 4)] + [(q, ilp) for q in (1, 2, 4, 8) for ilp in (1, 2, 4)]
+    try:
+        rows, (vd, vi) = oracle.refgpu_sweep(centroids, codes, queries, s["k"], points, reps=5)
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": str(e)}
+    nq = queries.shape[0]
+
+    def summary(r):
+        return {"queries/s": round(nq / (r["total_ms"] / 1e3), 1), "total_ms": round(r["total_ms"], 4),
+                "scan_ms": round(r["scan_ms"], 4), "lut_ms": round(r["lut_ms"], 4),
+                "select_ms": round(r["select_ms"], 4), "transfer_ms": round(r["transfer_ms"], 4),
+                "queries_per_block": int(r["queries_per_block"]), "ilp": int(r["vectors_per_step"]),
+                "blocks_x": int(r["blocks_x"]), "grid_y": int(r["grid_y"])}
+    best = min(rows[1:], key=lambda r: r["total_ms"])
+    out = {"device": name, "default_tuning": summary(rows[0]), "best_of_sweep": summary(best),
+           "sweep_points": len(points) - 1}
+    if cpu_res is not None:
+        q0, (cd, ci) = cpu_res
+        out["ids_equal_cpu"] = round(float(np.mean(vi[q0:q0 + ci.shape[0]] == ci)), 6)
+        out["ids_equal_cpu_queries"] = int(ci.shape[0])
+    return out
 
 
 def finite(x):
@@ -285,6 +387,127 @@ def workload_name(s, cfg):
 
 
 # ------------------------------------------------------------------------------------------------ our arm
+def wavefront_floor(codes_sample: np.ndarray, perm: np.ndarray, Q: int, lookups: float, sm_count: int,
+                    sm_mhz: float):
+    """(wavefronts per fetch in the index's placement, the same in row order, floor ms) of a full scan: the
+    conflict-inclusive shared-memory wavefronts of `lookups` lookup-adds at one wavefront per clock per SM."""
+    full = codes_sample.shape[0] // 64 * 64
+    placed = np.concatenate([codes_sample[(np.arange(full) & ~63) + perm[:full]], codes_sample[full:]])
+    wf = lookup_wavefront_model(placed, Q)
+    wf_rows = lookup_wavefront_model(codes_sample, Q)
+    per_fetch = 4 if Q >= 4 else Q  # lookups served per warp LUT fetch per lane
+    floor_ms = lookups / 32.0 / per_fetch * wf / (sm_count * sm_mhz * 1e6) * 1e3
+    return wf, wf_rows, floor_ms
+
+
+def run_sharded(args, rank: int, world: int, local: int, stream, flush):
+    """A generated configuration (default c3: 100M rows, m 16, nq 10,000, k 10) sharded contiguously by id over the
+    run's ranks, each shard's codes generated on its GPU: every rank searches its shard, the per-shard top-k lists are
+    all-gathered over NCCL and merged on the GPU. Every rank takes the same collective steps; rank 0 returns the
+    block of the JSON line (None elsewhere). Steps are timed with CUDA events on the launching stream, L2 flushed
+    before each, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from veckern_b200 import PQSearcher, Tuning, configs, data, device_info, merge_topk_device
+    from veckern_b200.shard import gather_and_merge, shard_of
+
+    name = args.sharded
+    w = configs.make(name)
+    spec = w.spec
+    n, m, nq, k = spec["n"], spec["m"], spec["nq"], spec["k"]
+    sh = shard_of(n, world, rank)
+    tuning = Tuning(queries_per_block=args.qpb, vectors_per_step=args.ilp)
+    s = PQSearcher.generated(w.centroids, spec["code_seed"], w.cdf, sh.lo, sh.rows, device=local, id_base=sh.lo)
+    s.set_tuning(tuning)
+    d_q = torch.from_numpy(w.queries).cuda()
+    d_local = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+    d_gather = torch.empty((world, nq, k), dtype=torch.int64, device="cuda") if world > 1 else None
+    d_final = torch.empty((nq, k), dtype=torch.int64, device="cuda") if world > 1 else d_local
+
+    def exchange():
+        def merge(buf, lay):
+            merge_topk_device(local, buf, nq, lay["lists"], lay["k_in"], lay["query_stride"], lay["list_stride"], k,
+                              d_final, stream)
+        gather_and_merge(d_local, d_gather, nq, k, lambda buf, x: dist.all_gather_into_tensor(buf, x), merge)
+
+    for _ in range(args.sharded_warmup):
+        s.search_device(d_q, k, d_local, stream)
+        if world > 1:
+            exchange()
+    s.sync(stream)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.sharded_steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for e in evs:
+        flush.zero_()
+        e[0].record(stream)
+        s.search_device(d_q, k, d_local, stream)
+        e[1].record(stream)
+        if world > 1:
+            exchange()
+        e[2].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s.sync(stream)
+    clk = clocks.stop()
+    total = sum(a.elapsed_time(c) for a, b, c in evs)
+    search = sum(a.elapsed_time(b) for a, b, c in evs)
+    t = torch.tensor([total, search, -search], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_max, search_max, search_min = t[0].item(), t[1].item(), -t[2].item()
+
+    verified = None
+    if world > 1 and not args.no_verify:
+        if rank == 0:  # one GPU over the whole database: the merged result must be identical
+            with PQSearcher.generated(w.centroids, spec["code_seed"], w.cdf, 0, n, device=local) as one:
+                one.set_tuning(tuning)
+                ref = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+                one.search_device(d_q, k, ref, stream)
+                one.sync(stream)
+            verified = bool(torch.equal(ref, d_final))
+        dist.barrier()
+        if rank == 0 and not verified:
+            raise SystemExit(f"{name}: multi-GPU merged result differs from the single-GPU search")
+
+    out = None
+    if rank == 0:
+        K = max(1, args.sharded_steps)
+        info = device_info(local)
+        sm_mhz = clk.get("sm_mhz") or info.clock_mhz
+        search_ms = search_max / K
+        Q = min(args.qpb, 8)
+        sample = data.gen_codes(spec["code_seed"], w.cdf, sh.lo, min(1 << 17, sh.rows))
+        wf, wf_rows, floor_ms = wavefront_floor(sample, s.get_placement(sample.shape[0]), Q,
+                                                float(nq) * sh.rows * m, info.sm_count, sm_mhz)
+        out = {"workload": workload_name(spec, name) + f", sharded by id over {world} GPU(s)",
+               "metric": "queries/s", "value": round(nq / (total_max / K / 1e3), 2), "unit": "queries/s",
+               "ms_per_step": round(total_max / K, 3), "steps": args.sharded_steps, "warmup": args.sharded_warmup,
+               "shards": world, "rows_per_gpu": sh.rows, "queries_per_block": tuning.queries_per_block,
+               "search_ms_per_gpu": {"max": round(search_max / K, 3), "min": round(search_min / K, 3)},
+               "exchange_ms": round((total_max - search_max) / K, 3) if world > 1 else 0.0,
+               "lookup_floor": {"wavefronts_per_fetch": round(wf, 3), "wavefronts_per_fetch_row_order": round(wf_rows, 3),
+                                "floor_ms_per_gpu": round(floor_ms, 3),
+                                "frac": round(floor_ms / search_ms, 4),
+                                "note": "full scan's conflict-inclusive shared-memory wavefronts of this shard at one "
+                                        "per clock per SM, against the per-GPU search time (LUT + pruned scan + "
+                                        "list merge)"},
+               "hbm": {"code_bytes_per_gpu": int(sh.rows * m),
+                       "traffic": ncu_traffic(name, sh.rows, m, nq, k), "peak_gbs_measured": _peak("hbm_gbs")},
+               "verified_against_single_gpu": verified, "clocks": clk,
+               "l2": "flushed (256 MB write) before every timed step"}
+    s.close()
+    del d_q, d_local, d_gather, d_final
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -404,7 +627,7 @@ def run_ours(args):
     clk = clocks.stop()
 
     verified = None
-    if args.verify and world > 1:
+    if not args.no_verify and world > 1:
         # the gathered + merged result of the last device step against one GPU over the whole database
         s.search_device(d_q, k, d_local, stream)
         exchange()
@@ -441,7 +664,6 @@ def run_ours(args):
         achieved = lookups / (scan_mean / 1e3)
         smem_peak_bytes = 128.0 * info.sm_count * sm_mhz * 1e6
         Q = s.last_launch().queries_per_block
-        wf = wf_rows = None
         sample = 1 << 17
         if w.codes is not None:
             rows_codes = w.codes[:sample]
@@ -449,19 +671,13 @@ def run_ours(args):
             from veckern_b200 import data as vkdata
             rows_codes = vkdata.gen_codes(spec["code_seed"], w.cdf, lo, min(sample, hi - lo))
         # the device layout: rows of whole 64-row windows in the index's lane placement
-        perm = s.get_placement(rows_codes.shape[0])
-        full = rows_codes.shape[0] // 64 * 64
-        placed = np.concatenate([rows_codes[(np.arange(full) & ~63) + perm[:full]], rows_codes[full:]])
-        wf = lookup_wavefront_model(placed, Q)
-        wf_rows = lookup_wavefront_model(rows_codes, Q)
-        per_fetch = 4 if Q >= 4 else Q  # lookups served per warp LUT fetch per lane
-        fetches = lookups / 32.0 / per_fetch
-        floor_ms = fetches * wf / (info.sm_count * sm_mhz * 1e6) * 1e3 if wf else None
+        wf, wf_rows, floor_ms = wavefront_floor(rows_codes, s.get_placement(rows_codes.shape[0]), Q, lookups,
+                                                info.sm_count, sm_mhz)
         roofline = {
             "bound": "smem",
             "achieved": round(achieved * 4 / 1e9, 1), "peak": round(smem_peak_bytes / 1e9, 1), "unit": "GB/s",
             "frac": round(achieved * 4 / smem_peak_bytes, 4),
-            "traffic": ncu_traffic(args.config, spec, world),
+            "traffic": ncu_traffic(args.config, hi - lo, m, nq, k),
             "note": ("achieved = algorithmic LUT bytes (4 B per (query, row, sub-space) lookup, nq*n*m per launch) / "
                      "scan-kernel event time; peak = shared-memory bandwidth 128 B/clk/SM x SMs x median SM clock "
                      "sampled under load. lookup_floor: time the full scan's conflict-inclusive LDS wavefronts need "
@@ -478,6 +694,11 @@ def run_ours(args):
             "hbm": {"code_bytes_per_launch": int((hi - lo) * m), "peak_gbs_measured": _peak("hbm_gbs")},
         }
         cpu = None if args.no_cpu_baseline else cpu_baseline(args, w, spec)
+    sharded = None
+    if args.sharded not in ("none", args.config):
+        s.close()
+        sharded = run_sharded(args, rank, world, local, stream, flush)
+    if rank == 0:
         line = {
             "metric": "queries/s", "value": round(value, 1), "unit": "queries/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
@@ -497,6 +718,7 @@ def run_ours(args):
             "gpu_launches": args.steps * (3 + (1 if world > 1 else 0)),
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
             "verified_against_single_gpu": verified,
+            "sharded": sharded,
         }
         print(json.dumps(finite(line)), flush=True)
     if world > 1:
@@ -517,7 +739,7 @@ def cpu_baseline(args, w, spec):
 
     if int(os.environ.get("WORLD_SIZE", 1)) > 1:
         return None
-    cores = os.cpu_count() or 1
+    cores = usable_cores()
     if w.codes is None:  # generated database: the C port streams host-regenerated codes for one query
         from veckern_b200 import data
         P = oracle.port()
@@ -535,6 +757,7 @@ def cpu_baseline(args, w, spec):
     kind = "reference" if oracle.ref_available() else "port"
     if kind == "reference":
         R = oracle.ref()
+        cores = R.set_threads(cores)
         pq = R.pq(spec["d"], spec["m"])
         pq.centroids = w.centroids
         run = lambda q: R.adc_search(pq, w.codes, q, spec["k"])  # noqa: E731

@@ -221,10 +221,13 @@ int vk_gen_codes_device(int device, uint64_t seed, const uint32_t* cdf, int clus
  * the search's working memory (LUTs, per-chunk lists, pruning state) lives in one fixed array of
  * VK_NOALLOC_SCRATCH_BYTES compiled into the library, which every GPU that loads the library holds until the
  * process exits. Calls needing more than that (about nq * m KiB of LUTs plus nq * k * (chunks + 2) * 8 bytes of
- * lists) are rejected with VK_ERR_INVALID; split the queries. The first call on a device looks the array's
- * address up (make that first call before any stream capture). Runs on `stream` (NULL = the default stream) and
- * returns when the results are written. All calls share the one array: calls that overlap on the GPU (other host
- * threads, other streams) race and must not be made. */
+ * lists) are rejected with VK_ERR_INVALID; split the queries. The array's device address is looked up when the
+ * first index is created on a device, not during a search. Make one warm-up call per index and per search shape
+ * (k, tuning, query count class) before serving: the CUDA runtime loads a kernel's code on its first launch (lazy
+ * module loading, the CUDA 12 default), and that load may allocate device memory. Runs on `stream` (NULL = the
+ * default stream) and is synchronous: it returns when the results are written and the kernels' status is read.
+ * All calls share the one array, which keeps the previous call's contents (each call resets what must start at
+ * zero): calls that overlap on the GPU (other host threads, other streams) race and must not be made. */
 #define VK_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
 int vk_search_noalloc(vk_index_t* index, const float* d_queries, int64_t nq, int k, const vk_tuning_t* tuning,
                       vk_neighbor_t* d_out, void* stream);

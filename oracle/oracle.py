@@ -162,6 +162,14 @@ class Ref:
         L.ref_topk_push_all.argtypes = [_f32p, _i32p, _i64, _i64, _f32p, _i32p]
         L.ref_rerank_exact.argtypes = [_f32p, _i64, _f32p, _i64, _i32p, _i64, _i64, _f32p, _i32p]
         L.ref_synthetic_clustered.argtypes = [_i64, _i64, _i64, C.c_uint64, _f32p]
+        L.ref_set_threads.argtypes = [C.c_int]
+        L.ref_get_threads.restype = C.c_int
+
+    def set_threads(self, n: int) -> int:
+        """OpenMP threads of the reference's parallel loops (overrides an inherited OMP_NUM_THREADS); returns the
+        count now in effect."""
+        self.lib.ref_set_threads(int(n))
+        return int(self.lib.ref_get_threads())
 
     class PQ:
         def __init__(self, lib, d, m):
@@ -285,3 +293,36 @@ def ref() -> Ref:
 
 def set_threads(n: int) -> None:
     os.environ["OMP_NUM_THREADS"] = str(n)
+
+
+REFGPU_SO = HERE / "_ref" / "libveckern_refgpu.so"
+
+
+def refgpu_available() -> bool:
+    return REFGPU_SO.exists()
+
+
+def refgpu_sweep(centroids, codes, queries, k, points, reps=5):
+    """The reference's own v8 kernel (FusedWarp through its veckern::gpu::PQSearcher, compiled for sm_100a) on
+    these inputs: for each (queries_per_block, ilp) in `points`, median stage times of `reps` searches after one
+    warm-up. Returns (rows: list of dicts, (dists, ids) of the first point)."""
+    L = C.CDLL(str(REFGPU_SO))
+    L.refgpu_sweep.argtypes = [_f32p, _i64, _i64, _u8p, _i64, _f32p, _i64, _i64, _i32p, _i32p, C.c_int, C.c_int,
+                               np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS"), _f32p, _i32p]
+    L.refgpu_last_error.restype = C.c_char_p
+    centroids = _f32(centroids)
+    m, _, dsub = centroids.shape
+    codes = _u8(codes)
+    queries = _f32(queries).reshape(-1, m * dsub)
+    nq = queries.shape[0]
+    qs = np.array([p[0] for p in points], np.int32)
+    ilps = np.array([p[1] for p in points], np.int32)
+    out = np.zeros((len(points), 10), np.float64)
+    d = np.empty((nq, k), np.float32)
+    i = np.empty((nq, k), np.int32)
+    if L.refgpu_sweep(centroids, m * dsub, m, codes, codes.shape[0], queries, nq, k, qs, ilps, len(points), reps,
+                      out, d, i) != 0:
+        raise RuntimeError("reference GPU search failed: " + L.refgpu_last_error().decode(errors="replace"))
+    keys = ("total_ms", "transfer_ms", "lut_ms", "scan_ms", "select_ms", "threads", "blocks_x", "grid_y",
+            "queries_per_block", "vectors_per_step")
+    return [dict(zip(keys, (float(x) for x in row))) for row in out], (d, i)

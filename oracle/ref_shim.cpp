@@ -5,6 +5,8 @@
 // It lets Python tests and bench.py's CPU-baseline leg call the reference itself: to pin the plain-C
 // restatement (oracle/vk_oracle.c), to generate the golden fixtures under tests/golden/, and to time the
 // reference CPU path. Nothing in the product loads it.
+#include <omp.h>
+
 #include <cstdint>
 #include <cstring>
 #include <vector>
@@ -26,6 +28,13 @@ void split(const std::vector<Neighbor>& nb, float* d, int32_t* i) {
 }  // namespace
 
 extern "C" {
+
+// OpenMP threads for the reference's parallel loops (its CPU path, PQ training and encoding). A launcher may have
+// set OMP_NUM_THREADS=1 before the process started (torchrun does); this overrides it for the calling thread.
+void ref_set_threads(int n) {
+    if (n > 0) omp_set_num_threads(n);
+}
+int ref_get_threads() { return omp_get_max_threads(); }
 
 void* ref_pq_create(int64_t d, int64_t m) { return new ProductQuantizer(d, m); }
 void ref_pq_destroy(void* pq) { delete static_cast<ProductQuantizer*>(pq); }

@@ -1,10 +1,12 @@
 """GPU: the five BASELINE.json configurations at full size, bit-exact against the CPU oracle.
 
-c0: every query against the oracle. c1 (m = 16, 32, 64) and c2 (k = 100): all queries searched on the GPU, a
-fixed sample of them against the oracle. c3 (100M rows) and c4 (1B rows), generated on the GPU: every returned
-distance is recomputed on the host from independently regenerated codes (exact ADC sum), results are ascending,
-a split of the database into id-offset shards merged on the GPU gives the same result, and sampled queries are
-checked against the oracle streaming the host-regenerated database.
+c0, c1 (m = 16, 32, 64) and c2 (k = 100, and the nq = 1 latency case): every query of the configuration against
+the oracle, under the planner's default tuning and under the benchmark's (Q = 8, ILP = 2). c3 (100M rows, all
+10,000 queries) and c4 (1B rows, 1,000 queries, k = 10 and 100), generated on the GPU: every returned distance is
+recomputed on the host from independently regenerated codes (exact ADC sum), results are ascending, a split of the
+database into id-offset shards merged on the GPU gives the same result, and sampled queries are checked against
+the oracle streaming the host-regenerated database (one pass at the largest k; a top-k list's first entries are
+the top-k' list for k' < k).
 """
 import numpy as np
 import pytest
@@ -20,6 +22,20 @@ def gpu_topk(cent, codes, q, k, qpb=4):
         s.set_tuning(Tuning(queries_per_block=qpb))
         out, _ = s.search(q, k)
     return out["dist"].copy(), out["id"].copy()
+
+
+def gpu_topk_tunings(cent, codes, q, k, tunings):
+    """[(dist, ids)] of one index searched under each tuning."""
+    res = []
+    with PQSearcher(cent, codes) as s:
+        for t in tunings:
+            s.set_tuning(t)
+            out, _ = s.search(q, k)
+            res.append((out["dist"].copy(), out["id"].copy()))
+    return res
+
+
+BENCH_TUNING = Tuning(queries_per_block=8, vectors_per_step=2)
 
 
 def exact_adc(port, cent, q, codes_of_ids):
@@ -42,21 +58,26 @@ def test_c0_full(port):
 
 @pytest.mark.parametrize("m", [16, 32, 64])
 def test_c1_full(port, m):
+    """All 1,000 queries of config 1 at each m, bit-exact against the oracle."""
     w = configs.make("c1", m=m, encode=data.gpu_encoder())
-    d, i = gpu_topk(w.centroids, w.codes, w.queries, w.k, qpb=4 if m <= 32 else 2)
-    sample = np.arange(0, w.queries.shape[0], 16)
-    ed, ei = port.adc_search(w.centroids, w.codes, w.queries[sample], w.k)
-    assert_same_topk(d[sample], i[sample], ed, ei, f"c1 m={m}")
+    assert w.queries.shape[0] == 1000
+    ed, ei = port.adc_search(w.centroids, w.codes, w.queries, w.k)
+    tunings = [Tuning(queries_per_block=4 if m <= 32 else 2), BENCH_TUNING,
+               Tuning(queries_per_block=8, vectors_per_step=2, early_abandon=False)]
+    for t, (d, i) in zip(tunings, gpu_topk_tunings(w.centroids, w.codes, w.queries, w.k, tunings)):
+        assert_same_topk(d, i, ed, ei, f"c1 m={m} {t}")
 
 
 def test_c2_full(port):
+    """All 1,000 queries of config 2 at k = 100, and the single-query latency case, against the oracle."""
     w = configs.make("c2", encode=data.gpu_encoder())
-    d, i = gpu_topk(w.centroids, w.codes, w.queries, 100)
-    sample = np.arange(0, w.queries.shape[0], 100)
-    ed, ei = port.adc_search(w.centroids, w.codes, w.queries[sample], 100)
-    assert_same_topk(d[sample], i[sample], ed, ei, "c2 k=100")
-    d1, i1 = gpu_topk(w.centroids, w.codes, w.queries[:1], 10)  # the single-query latency case
-    assert_same_topk(d1, i1, ed[:1, :10], ei[:1, :10], "c2 nq=1 k=10")
+    assert w.queries.shape[0] == 1000
+    ed, ei = port.adc_search(w.centroids, w.codes, w.queries, 100)
+    tunings = [Tuning(queries_per_block=4), BENCH_TUNING]
+    for t, (d, i) in zip(tunings, gpu_topk_tunings(w.centroids, w.codes, w.queries, 100, tunings)):
+        assert_same_topk(d, i, ed, ei, f"c2 k=100 {t}")
+    for t, (d1, i1) in zip(tunings, gpu_topk_tunings(w.centroids, w.codes, w.queries[:1], 10, tunings)):
+        assert_same_topk(d1, i1, ed[:1, :10], ei[:1, :10], f"c2 nq=1 k=10 {t}")
 
 
 def _generated_checks(port, name, nq, ks, oracle_queries, split):
@@ -66,6 +87,9 @@ def _generated_checks(port, name, nq, ks, oracle_queries, split):
     with PQSearcher.generated(w.centroids, s["code_seed"], w.cdf, 0, n) as idx:
         idx.set_tuning(Tuning(queries_per_block=4))
         results = {k: idx.search(w.queries, k)[0].copy() for k in ks}
+        idx.set_tuning(BENCH_TUNING)  # the benchmark's plan gives the same lists
+        for k in ks:
+            assert np.array_equal(idx.search(w.queries, k)[0].view(np.int64), results[k].view(np.int64)), k
     for k, out in results.items():
         d, i = out["dist"], out["id"]
         assert (i >= 0).all() and (i < n).all()
@@ -87,24 +111,25 @@ def _generated_checks(port, name, nq, ks, oracle_queries, split):
     merge_topk_device(0, gathered, nq, split, k, k, nq * k, k, merged)  # [shard][q][k]: query stride k
     torch.cuda.synchronize()
     assert np.array_equal(merged.cpu().numpy(), results[k].view(np.int64)), f"{name}: {split} merged shards differ"
-    # sampled queries against the oracle over the host-regenerated database
+    # sampled queries against the oracle over the host-regenerated database: one pass at the largest k
+    sample = np.array(oracle_queries)
+    lut = port.compute_lut(w.centroids, w.queries[sample])
+    block = 1 << 23
+    kmax = max(ks)
+
+    def blocks():
+        for a in range(0, n, block):
+            yield data.gen_codes(s["code_seed"], w.cdf, a, min(block, n - a)), a
+
+    ed, ei = port.stream_search(lut, blocks(), kmax)
     for k in ks:
-        sample = np.array(oracle_queries)
-        lut = port.compute_lut(w.centroids, w.queries[sample])
-        block = 1 << 23
-
-        def blocks():
-            for a in range(0, n, block):
-                yield data.gen_codes(s["code_seed"], w.cdf, a, min(block, n - a)), a
-
-        ed, ei = port.stream_search(lut, blocks(), k)
         out = results[k]
-        assert_same_topk(out["dist"][sample], out["id"][sample], ed, ei, f"{name} oracle k={k}")
+        assert_same_topk(out["dist"][sample], out["id"][sample], ed[:, :k], ei[:, :k], f"{name} oracle k={k}")
 
 
 def test_c3_full(port):
-    _generated_checks(port, "c3", nq=10_000, ks=[10], oracle_queries=[0, 4_999, 9_999], split=4)
+    _generated_checks(port, "c3", nq=10_000, ks=[10], oracle_queries=[0, 1, 2_500, 4_999, 7_777, 9_999], split=4)
 
 
 def test_c4_full(port):
-    _generated_checks(port, "c4", nq=256, ks=[10, 100], oracle_queries=[0], split=2)
+    _generated_checks(port, "c4", nq=1_000, ks=[10, 100], oracle_queries=[0, 1, 333, 500, 998, 999], split=2)

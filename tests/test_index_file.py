@@ -101,3 +101,36 @@ def test_damage_is_detected(tmp_path):
         data.index_info(p)
     with pytest.raises(data.IndexFileError, match="cannot open"):
         data.index_info(tmp_path / "missing.vkpq")
+
+
+def test_crafted_headers_with_valid_checksums_are_rejected(tmp_path):
+    """Headers whose own CRC-32C is right but whose sizes would wrap 64-bit offset arithmetic (or ask for absurd
+    shapes) are refused before any buffer is sized from them."""
+    cent, codes = make(1000, 16, 8, seed=4)
+    good = tmp_path / "good.vkpq"
+    data.write_index(good, cent, codes)
+    raw = bytearray(good.read_bytes())
+
+    def forged(name, **fields):
+        b = bytearray(raw)
+        layout = {"n": (16, 8), "d": (24, 4), "m": (28, 4), "dsub": (32, 4), "codes_off": (48, 8),
+                  "block_rows": (56, 8), "crc_off": (64, 8)}
+        for k, v in fields.items():
+            off, size = layout[k]
+            b[off:off + size] = int(v).to_bytes(size, "little")
+        b[76:80] = data.crc32c(bytes(b[:76])).to_bytes(4, "little")  # re-sign the header
+        p = tmp_path / name
+        p.write_bytes(bytes(b))
+        return p
+
+    bad = [
+        forged("wrap_n.vkpq", n=(1 << 64) // 16 + 1),                          # n * m wraps to a small number
+        forged("huge_m.vkpq", m=1 << 30, dsub=4, d=0),                          # m * dsub = 2^32 wraps to 0 in 32 bits
+        forged("huge_blocks.vkpq", block_rows=1),                               # fine shape, crc section past the end
+        forged("wrap_off.vkpq", codes_off=(1 << 64) - 4096),                   # offset + size wraps
+        forged("wrap_crc.vkpq", crc_off=(1 << 64) - 8),
+    ]
+    for p in bad:
+        with pytest.raises(data.IndexFileError):
+            data.index_info(p)
+    assert data.index_info(forged("resigned.vkpq")) == {"n": 1000, "d": 128, "m": 16, "dsub": 8}

@@ -134,3 +134,24 @@ def test_rerank_port_matches_reference_with_duplicates():
         rd, ri = R.rerank_exact(base, q, cand, k)
         pd, pi = oracle.port().rerank_exact(base, q, cand, k)
         assert_same_topk(pd, pi, rd, ri, f"rerank k={k}")
+
+
+def test_reference_arm_inputs_match_the_package():
+    """bench.py's reference arm builds its workload without this repository's libraries (numpy generators + the
+    reference's own ProductQuantizer); it must be the very workload the package's arm searches."""
+    from oracle import inputs
+    from veckern_b200 import configs, data
+
+    for seed, row0 in ((0, 0), (3, 0), (0, 777_777)):
+        a = inputs.gen_mixture(0, seed, 3_000, 128, row0=row0)
+        assert np.array_equal(bits(a), bits(data.gen_mixture(0, seed, 3_000, 128, row0=row0)))
+    assert np.array_equal(bits(inputs.gen_normal(2, 500, 128, row0=5)), bits(data.gen_normal(2, 500, 128, row0=5)))
+    if not oracle.ref_available():
+        pytest.skip("reference library not built")
+    for name, n in (("c0", 30_000), ("c1", 30_000)):
+        spec = configs.spec(name, n=n, nq=50)
+        pq, codes, q = inputs.reference_workload(spec, oracle.ref())
+        w = configs.make(name, n=n, nq=50)
+        assert np.array_equal(bits(pq.centroids), bits(w.centroids)), name
+        assert np.array_equal(codes, w.codes), name
+        assert np.array_equal(bits(q), bits(w.queries)), name

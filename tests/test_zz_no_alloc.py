@@ -4,7 +4,8 @@ It is for callers that must not call cudaMalloc/cudaFree during a search (an all
 device and stall other streams, or the process has handed its memory to its own allocator): its working memory is
 one fixed array inside the library. Called through the C ABI, its results must equal the allocating device-path
 entry point's exactly (the same bit-exact contract), on two calls in a row, because the array keeps the previous
-call's contents. This file is collected last on purpose.
+call's contents; the second call must leave the device's free memory unchanged. This file is collected last on
+purpose.
 """
 import ctypes as C
 
@@ -36,12 +37,35 @@ def test_noalloc_matches_allocating_entry_point_twice(golden):
             s.search_device(d_q, k, ref, None, tuning=tuning)
             s.sync(None)
             rd, ri = (x.cpu().numpy() for x in device_result_split(ref))
+            outs = [torch.full((d_q.shape[0], k), -1, dtype=torch.int64, device="cuda") for _ in range(2)]
+            torch.cuda.synchronize()
             for call in range(2):
-                out = torch.full((d_q.shape[0], k), -1, dtype=torch.int64, device="cuda")
-                assert _noalloc(s, d_q, k, tuning, out) == N.VK_OK, N.last_error()
-                od, oi = (x.cpu().numpy() for x in device_result_split(out))
+                free_before = torch.cuda.mem_get_info()[0]
+                assert _noalloc(s, d_q, k, tuning, outs[call]) == N.VK_OK, N.last_error()
+                if call == 1:  # after the first call (kernel code loaded), a call takes no device memory
+                    assert torch.cuda.mem_get_info()[0] == free_before, "vk_search_noalloc changed free memory"
+                od, oi = (x.cpu().numpy() for x in device_result_split(outs[call]))
                 assert_same_topk(od, oi, rd, ri, f"no-alloc call {call} k={k}")
             assert_same_topk(od, oi, g[f"d_k{k}"], g[f"i_k{k}"], "no-alloc vs reference fixture")
+
+
+def test_noalloc_single_query_wide_merge(golden):
+    """One query over many chunk lists: the few-query merge (one block per query), as on the allocating path."""
+    import torch
+
+    g = golden("gpu_fixture")
+    with PQSearcher(g["centroids"], g["codes"]) as s:
+        d_q = torch.from_numpy(g["queries"][:1].copy()).cuda()
+        for k in (100, 10):
+            ref = torch.empty((1, k), dtype=torch.int64, device="cuda")
+            s.search_device(d_q, k, ref, None, tuning=Tuning())
+            s.sync(None)
+            rd, ri = (x.cpu().numpy() for x in device_result_split(ref))
+            for call in range(2):
+                out = torch.full((1, k), -1, dtype=torch.int64, device="cuda")
+                assert _noalloc(s, d_q, k, Tuning(), out) == N.VK_OK, N.last_error()
+                od, oi = (x.cpu().numpy() for x in device_result_split(out))
+                assert_same_topk(od, oi, rd, ri, f"no-alloc nq=1 call {call} k={k}")
 
 
 def test_noalloc_rejects_work_beyond_its_array(golden):

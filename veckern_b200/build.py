@@ -40,7 +40,8 @@ def _nvcc() -> str:
 
 
 def _headers() -> list[Path]:
-    return sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(INCLUDE.rglob("*.h*"))
+    return (sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted((CSRC / "host").glob("*.h"))
+            + sorted(INCLUDE.rglob("*.h*")))
 
 
 def _stale(target: Path, deps: list[Path]) -> bool:

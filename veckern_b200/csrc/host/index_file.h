@@ -146,12 +146,20 @@ inline std::string decode_header(const uint8_t* b, uint64_t file_bytes, Header& 
     h.crc_off = get64(b, 64);
     h.centroids_crc = get32(b, 72);
     h.header_crc = get32(b, 76);
-    if (h.m == 0 || h.dsub == 0 || h.d != h.m * h.dsub || h.ksub != 256 || h.block_rows == 0)
+    // Bound every field before any arithmetic on it, so that no product or sum below can wrap: a header whose own
+    // checksum is right may still have been written with nonsense values.
+    if (h.m == 0 || h.m > 4096 || h.dsub == 0 || h.dsub > 4096 || h.n >= (uint64_t(1) << 31) ||
+        (uint64_t)h.d != (uint64_t)h.m * h.dsub || h.ksub != 256 || h.block_rows == 0 ||
+        h.block_rows > (uint64_t(1) << 31))
         return "inconsistent shape in header";
-    const uint64_t cbytes = (uint64_t)h.m * 256u * h.dsub * 4u;
+    if (h.centroids_off > file_bytes || h.codes_off > file_bytes || h.crc_off > file_bytes)
+        return "file truncated or section offsets out of range";
+    const uint64_t cbytes = (uint64_t)h.m * 256u * h.dsub * 4u;  // < 2^35
+    const uint64_t code_bytes = h.n * h.m;                          // < 2^43
     const uint64_t blocks = (h.n + h.block_rows - 1) / h.block_rows;
+    // every offset is at most file_bytes (< 2^63), every size below 2^44: the sums cannot wrap
     if (h.centroids_off < kHeaderBytes || h.centroids_off + cbytes > h.codes_off ||
-        h.codes_off + h.n * h.m > h.crc_off || h.crc_off + blocks * 4u > file_bytes)
+        h.codes_off + code_bytes > h.crc_off || h.crc_off + blocks * 4u > file_bytes)
         return "file truncated or section offsets out of range";
     return "";
 }

@@ -240,6 +240,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
     const int items = a.groups * a.chunks;
     const int64_t tile_rows = 32 * ILP;
     uint32_t issued = 0, consumed = 0, lut_phase = 0;  // issued: lane 0 only
+    uint32_t lut_pending = ~0u;  // thread 0: parity of a LUT copy not yet seen complete (~0u: none)
     int cur_g = -1;
 
     for (;;) {
@@ -262,11 +263,14 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                     const uint32_t len = min(32768u, plan.lut_bytes - off);
                     bulk_g2s(lut_smem + off, src + off, len, lut_bar);
                 }
+                lut_pending = lut_phase;
             }
             // Vote, so that the warp's lanes take the same path even if only some of them ran out of time.
             if (!__all_sync(FULL, mbar_wait_bounded(lut_bar, lut_phase, a.wait_budget))) {
                 if (lane == 0) atomicOr(a.status, ERR_WAIT_TIMEOUT);
                 *s_abort = 1;
+            } else if (threadIdx.x == 0) {
+                lut_pending = ~0u;
             }
             lut_phase ^= 1u;
             cur_g = g;
@@ -536,7 +540,8 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
             // Let this warp's copies still in flight land before the block can exit.
             while (consumed < issued) {
                 const uint32_t slot = consumed % (uint32_t)a.stages;
-                mbar_wait_bounded(my_bars + slot, (consumed / (uint32_t)a.stages) & 1u, a.wait_budget);
+                if (!mbar_wait_bounded(my_bars + slot, (consumed / (uint32_t)a.stages) & 1u, 4 * a.wait_budget))
+                    atomicOr(a.status, ERR_DRAIN_TIMEOUT);
                 ++consumed;
             }
         }
@@ -611,6 +616,10 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
             }
         }
     }
+    // A LUT copy whose wait ran out may still be in flight: it must land before the block's shared memory is
+    // released.
+    if (threadIdx.x == 0 && lut_pending != ~0u && !mbar_wait_bounded(lut_bar, lut_pending, 4 * a.wait_budget))
+        atomicOr(a.status, ERR_DRAIN_TIMEOUT);
 }
 
 // ------------------------------------------------------------------------------------------------ merge

@@ -410,6 +410,15 @@ int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk
     return VK_OK;
 }
 
+int status_error(int status) {
+    if (status & vk::ERR_DRAIN_TIMEOUT)
+        return fail(VK_ERR_DEVICE,
+                    "kernel reported status 0x%x: a bounded wait ran out and the kernel could not confirm that its "
+                    "own copies had finished; treat this device's CUDA context as unusable",
+                    status);
+    return fail(VK_ERR_DEVICE, "kernel reported status 0x%x (a bounded wait ran out)", status);
+}
+
 int read_status(vk_index* ix, cudaStream_t st) {
     int status = 0;
     VK_TRY_CUDA(cudaMemcpyAsync(&status, ix->flags + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
@@ -417,7 +426,7 @@ int read_status(vk_index* ix, cudaStream_t st) {
     if (status != 0) {
         VK_TRY_CUDA(cudaMemsetAsync(ix->flags + 1, 0, sizeof(int), st));
         VK_TRY_CUDA(cudaStreamSynchronize(st));
-        return fail(VK_ERR_DEVICE, "kernel reported status 0x%x (a bounded wait ran out)", status);
+        return status_error(status);
     }
     return VK_OK;
 }
@@ -427,6 +436,35 @@ int64_t max_query_batch(const vk_index* ix) {
     const int64_t by_lut = std::max<int64_t>(8, (int64_t)(kLutBudgetBytes / ((size_t)ix->m * vk::KSUB * 4)));
     return std::min<int64_t>(by_lut, 65528) / 8 * 8;
 }
+
+// ------------------------------------------------------------------------------------------------ no allocation
+// Working memory of vk_search_noalloc: one fixed array in the library's device image instead of the index's
+// cudaMalloc'd buffers. Host code cannot use the array's name as a device address (in host code it names a
+// host-side stand-in); the address is looked up per device with cudaGetSymbolAddress, the device current, when the
+// first index is created on that device, and cached. Nothing on vk_search_noalloc's path calls cudaMalloc, cudaFree
+// or any allocating routine.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[VK_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mutex;
+constexpr int kNoAllocMaxDevices = 64;
+unsigned char* g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+// The array's device address on `device`, which must be the current device.
+int noalloc_scratch_address(int device, unsigned char** out) {
+    if (device < 0 || device >= kNoAllocMaxDevices) return fail(VK_ERR_UNSUPPORTED, "device %d out of range", device);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_addr[device]) {
+        void* addr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+        if (e != cudaSuccess)
+            return fail(VK_ERR_CUDA, "cudaGetSymbolAddress(scratch) on device %d failed: %s", device, cudaGetErrorString(e));
+        g_noalloc_addr[device] = static_cast<unsigned char*>(addr);
+    }
+    *out = g_noalloc_addr[device];
+    return VK_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 int create_common(int device, const float* centroids, int m, int dsub, int64_t n, int64_t id_base,
                   vk_index** out, vk_index*& ix) {
@@ -463,6 +501,8 @@ int create_common(int device, const float* centroids, int m, int dsub, int64_t n
     VK_TRY_CUDA(cudaMalloc(&ix->codes, (size_t)ix->n_pad * ix->W * sizeof(uint4)));
     VK_TRY_CUDA(cudaMemsetAsync(ix->codes, 0, (size_t)ix->n_pad * ix->W * sizeof(uint4), ix->stream));
     VK_TRY_CUDA(cudaMalloc(&ix->perm, (size_t)ix->n_pad));
+    unsigned char* scratch = nullptr;  // vk_search_noalloc's array: its address is resolved here, not at a search
+    VK_TRY(noalloc_scratch_address(device, &scratch));
     return VK_OK;
 }
 
@@ -1292,37 +1332,6 @@ int vk_gen_codes_device(int device, uint64_t seed, const uint32_t* cdf, int clus
 
 }  // extern "C"
 
-// ------------------------------------------------------------------------------------------------ no allocation
-// vk_search_noalloc: the search with its working memory in g_noalloc_scratch instead of the index's buffers.
-// Host code cannot use the array's name as a device address; its address is looked up per device with
-// cudaGetSymbolAddress (the device current) and cached. Nothing here calls cudaMalloc, cudaFree or any
-// allocating routine.
-namespace {
-
-static __device__ __align__(256) unsigned char g_noalloc_scratch[VK_NOALLOC_SCRATCH_BYTES];
-
-std::mutex g_noalloc_mutex;
-constexpr int kNoAllocMaxDevices = 64;
-unsigned char* g_noalloc_addr[kNoAllocMaxDevices] = {};
-
-int noalloc_scratch_address(int device, unsigned char** out) {
-    if (device < 0 || device >= kNoAllocMaxDevices) return fail(VK_ERR_UNSUPPORTED, "device %d out of range", device);
-    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (!g_noalloc_addr[device]) {
-        void* addr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
-        if (e != cudaSuccess)
-            return fail(VK_ERR_CUDA, "cudaGetSymbolAddress(scratch) on device %d failed: %s", device, cudaGetErrorString(e));
-        g_noalloc_addr[device] = static_cast<unsigned char*>(addr);
-    }
-    *out = g_noalloc_addr[device];
-    return VK_OK;
-}
-
-size_t align256(size_t x) { return (x + 255) / 256 * 256; }
-
-}  // namespace
-
 extern "C" int vk_search_noalloc(vk_index_t* ix, const float* d_queries, int64_t nq, int k, const vk_tuning_t* tuning,
                                  vk_neighbor_t* d_out, void* stream) {
     if (!ix) return fail(VK_ERR_INVALID, "index must not be NULL");
@@ -1407,18 +1416,23 @@ extern "C" int vk_search_noalloc(vk_index_t* ix, const float* d_queries, int64_t
         VK_TRY_CUDA(cudaLaunchKernel(p.fn, dim3(p.grid), dim3(p.threads), args, p.smem, st));
     }
     {
-        const void* fn = merge_kernel_ptr(p.S);
+        // the same merge choice as vk_search_device: one 8-warp block per query for few queries over many lists
+        const bool wide = nq <= ix->sm_count && (int64_t)p.chunks * k >= 256;
+        const void* fn = wide ? merge_wide_kernel_ptr(p.S) : merge_kernel_ptr(p.S);
         const int2* in = part;
         int2* o = reinterpret_cast<int2*>(d_out);
         int lists = p.chunks, k_in = k, kk = k;
         int64_t qstride = (int64_t)p.chunks * k, lstride = k;
         void* args[] = {(void*)&in, (void*)&nq, (void*)&lists, (void*)&k_in, (void*)&qstride, (void*)&lstride,
                         (void*)&kk, (void*)&o};
-        VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)ceil_div(nq, 4)), dim3(128), args, 0, st));
+        if (wide)
+            VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)nq), dim3(256), args, 0, st));
+        else
+            VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)ceil_div(nq, 4)), dim3(128), args, 0, st));
     }
     int status = 0;
     VK_TRY_CUDA(cudaMemcpyAsync(&status, flags + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
     VK_TRY_CUDA(cudaStreamSynchronize(st));
-    if (status != 0) return fail(VK_ERR_DEVICE, "kernel reported status 0x%x (a bounded wait ran out)", status);
+    if (status != 0) return status_error(status);
     return VK_OK;
 }

@@ -16,8 +16,10 @@ constexpr int WARP = 32;
 constexpr unsigned FULL = 0xffffffffu;
 constexpr int32_t SENTINEL_ID = 0x7fffffff;  // empty list slot: loses to every real (dist, id) pair
 
-// Status-word bits written by kernels (atomicOr).
-enum : int { ERR_WAIT_TIMEOUT = 1, ERR_LAYOUT = 2 };
+// Status-word bits written by kernels (atomicOr). ERR_DRAIN_TIMEOUT: after a wait ran out, the block also failed to
+// see its own bulk copies land within a second, longer budget before exiting; such a copy may still write the
+// block's shared memory, so the host treats the context as suspect.
+enum : int { ERR_WAIT_TIMEOUT = 1, ERR_LAYOUT = 2, ERR_DRAIN_TIMEOUT = 4 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
