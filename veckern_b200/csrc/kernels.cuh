@@ -102,6 +102,18 @@ struct ScanArgs {
 struct ScanSmem {
     uint32_t lut, stage, scratch, queue, ring, bars, flags, total, tile_bytes, stage_bytes, lut_bytes;
 };
+// Pruned scan at m = 16: a (row, query) pair that survives phase A is queued together with its partial sum and its
+// remaining sub-codes (16 bytes), in a per-warp queue that persists across the item's tiles, so that phase B runs in
+// full batches of 32 pairs and the tile's stage buffer is released as soon as its survivors are queued. A tile with
+// more than CARRY_QWIDE survivors is finished with the Q-wide lookups instead (it always fits: full batches leave
+// fewer than 32 entries queued between tiles). Other m keep a per-tile queue of row indices into the stage buffer.
+constexpr int CARRY_CAP = 96;
+constexpr int CARRY_QWIDE = CARRY_CAP - 32;
+__host__ __device__ constexpr bool carry_queue(int m) { return m == 16; }
+// Rows of a pruned chunk, relative to its first 64-row window: 24 bits of a queue entry (with the query, 3 bits,
+// and the phase-A depth, 2 bits).
+constexpr int64_t CARRY_MAX_CHUNK_ROWS = int64_t(1) << 23;
+
 __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp, int nw, int stages, int k,
                                                    bool prune, int merge_slots) {
     auto up = [](uint32_t x, uint32_t a) { return (x + a - 1) / a * a; };
@@ -113,8 +125,11 @@ __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp,
     p.stage = up(p.lut_bytes, 128);
     p.scratch = up(p.stage + (uint32_t)nw * stages * p.stage_bytes, 128);
     p.queue = up(p.scratch + (uint32_t)merge_slots * nw * k * 8u, 16);
-    // the queue holds at most half a tile's (row, query) pairs: with more survivors the tile is finished in full
-    p.ring = up(p.queue + (prune ? (uint32_t)nw * 16u * ilp * Q * 8u : 0u), 16);
+    // m = 16: the carry queue (CARRY_CAP 16-byte entries per warp); other m: at most half a tile's (row, query)
+    // pairs, 8 bytes each (with more survivors the tile is finished in full)
+    const uint32_t queue_bytes = !prune ? 0u : carry_queue(m) ? (uint32_t)nw * CARRY_CAP * 16u
+                                                              : (uint32_t)nw * 16u * ilp * Q * 8u;
+    p.ring = up(p.queue + queue_bytes, 16);
     p.bars = up(p.ring + (uint32_t)nw * stages * 4u, 16);
     p.flags = p.bars + (uint32_t)(nw * stages + 1) * 8u;
     p.total = up(p.flags + 16, 128);
@@ -292,6 +307,65 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
         const int64_t t_begin = row_begin / tile_rows;
         const int ntiles = (int)(row_end / tile_rows - t_begin);
 
+        // Carry queue (PRUNE, m = 16): entry = {partial sum bits, rel | q << 24 | (depth - SA) / 2 << 27, sub-codes
+        // depth..15 as 8 bytes (sub-code `depth` lowest)}, rel = row - the chunk's first 64-row window, so that the
+        // row's id is carry_id0 + rel; qcnt is warp-uniform.
+        int qcnt = 0;
+        const int32_t carry_id0 = (int32_t)(a.id_base + (row_begin & ~(int64_t)(PLACE_WINDOW - 1)));
+        int4* my_carry = reinterpret_cast<int4*>(smem + plan.queue) + warp * CARRY_CAP;
+        // Finishes entries [start, start + count) (count <= 32), one pair per lane, two sub-spaces per step, each
+        // lane dropping out as soon as its sum exceeds its query's bound; offers the completed pairs.
+        auto carry_batch = [&](int start, int count) {
+            __syncwarp();  // entries written by other lanes are visible
+            const bool in = lane < count;
+            const int4 ent = in ? my_carry[start + lane] : make_int4(0, 0, 0, 0);
+            float x = __int_as_float(ent.x);
+            const uint32_t meta = (uint32_t)ent.y;
+            const int q = (int)((meta >> 24) & 7u);
+            int s = SA + 2 * (int)(meta >> 27);
+            uint32_t lo = (uint32_t)ent.z, hi = (uint32_t)ent.w;
+            // the query's bound now: min(the warp's view of its global bound, the warp list's k-th distance)
+            float bq = fminf(known[0], top[0].thr_d);
+#pragma unroll
+            for (int qq = 1; qq < Q; ++qq)
+                if (q == qq) bq = fminf(known[qq], top[qq].thr_d);
+            const unsigned char* lq = lut_smem + lut_query_base<Q>(q, MT);
+            bool live = in && !(x > bq);  // the bound may have dropped since the pair was queued
+#pragma unroll
+            for (int t = 0; t < (MT - SA) / 2; ++t) {
+                const bool go = live && s < MT;
+                if (!__any_sync(FULL, go)) break;
+                if (go) {
+                    const uint32_t c0 = lo & 0xffu, c1 = (lo >> 8) & 0xffu;
+                    lo = __funnelshift_r(lo, hi, 16);
+                    hi >>= 16;
+                    const float v0 = *reinterpret_cast<const float*>(lq + ((uint32_t)s * KSUB + c0) * lut_entry_bytes<Q>());
+                    const float v1 =
+                        *reinterpret_cast<const float*>(lq + ((uint32_t)(s + 1) * KSUB + c1) * lut_entry_bytes<Q>());
+                    x = __fadd_rn(x, v0);
+                    live = !(x > bq);
+                    x = __fadd_rn(x, v1);
+                    live = live && !(x > bq);
+                    s += 2;
+                }
+            }
+            if (__any_sync(FULL, live)) {  // usually every pair of the batch was abandoned
+                const int32_t id = carry_id0 + (int32_t)(meta & 0xffffffu);
+#pragma unroll
+                for (int qq = 0; qq < Q; ++qq) {
+                    if (__any_sync(FULL, live && q == qq)) top[qq].offer(x, id, live && q == qq, a.k);
+                }
+            }
+        };
+        // Runs the queue's full batches (all = true: every entry, at the end of the item).
+        auto carry_drain = [&](bool all) {
+            while (qcnt >= 32 || (all && qcnt > 0)) {
+                const int take = min(qcnt, 32);
+                qcnt -= take;
+                carry_batch(qcnt, take);
+            }
+        };
+
         // lane 0: take the chunk's next tile (if any) into the next ring slot
         auto refill = [&]() {
             const uint32_t slot = issued % (uint32_t)a.stages;
@@ -408,20 +482,18 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                     known[q] = fminf(known[q], __shfl_sync(FULL, gb, q));  // padded slots keep -1
                     bnd[q] = fminf(known[q], top[q].thr_d);
                 }
-                // ---- surviving (row, query) pairs
-                unsigned masks[ILP][Q];
+                // ---- surviving (row, query) pairs: this lane's pair (u, q) is alive while its partial sum is not
+                // above the query's bound (recomputed where needed rather than kept as ballots: registers)
+                auto alive = [&](int u, int q) {
+                    return tile_row0 + u * 32 + lane < a.n && !(acc[u][q] > bnd[q]);
+                };
                 int total = 0;
                 auto vote = [&]() {
                     total = 0;
 #pragma unroll
-                    for (int u = 0; u < ILP; ++u) {
-                        const bool valid = tile_row0 + u * 32 + lane < a.n;
+                    for (int u = 0; u < ILP; ++u)
 #pragma unroll
-                        for (int q = 0; q < Q; ++q) {
-                            masks[u][q] = __ballot_sync(FULL, valid && !(acc[u][q] > bnd[q]));
-                            total += __popc(masks[u][q]);
-                        }
-                    }
+                        for (int q = 0; q < Q; ++q) total += __popc(__ballot_sync(FULL, alive(u, q)));
                 };
                 vote();
                 // ---- deeper phase A while many pairs survive (warp-uniform: total comes from ballots)
@@ -435,11 +507,9 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                         vote();
                     }
                 });
-                int cnt = 0;
-                if (2 * total > 32 * ILP * Q) {
-                    // Most pairs survive (no tight bound yet), which the deepening above leaves possible only at
-                    // dep == SAX: finishing every row with the Q-wide lookups of the full scan is cheaper than
-                    // finishing pairs one query per lane.
+                // Finishes every row with the Q-wide lookups of the full scan (called only at dep == SAX) and
+                // offers the surviving pairs.
+                auto finish_qwide = [&]() {
                     static_for<MT - SAX>([&](auto e) { phase_a(Int<SAX + decltype(e)::value>{}); });
                     bool any = false;
                     int32_t ids[ILP];
@@ -447,25 +517,76 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                     for (int u = 0; u < ILP; ++u) {
                         ids[u] = row_id(u * 32 + lane);
 #pragma unroll
-                        for (int q = 0; q < Q; ++q) any |= ((masks[u][q] >> lane) & 1u) && top[q].admits(acc[u][q], ids[u]);
+                        for (int q = 0; q < Q; ++q) any |= alive(u, q) && top[q].admits(acc[u][q], ids[u]);
                     }
                     if (__any_sync(FULL, any)) {
 #pragma unroll
                         for (int u = 0; u < ILP; ++u)
 #pragma unroll
-                            for (int q = 0; q < Q; ++q) top[q].offer(acc[u][q], ids[u], (masks[u][q] >> lane) & 1u, a.k);
+                            for (int q = 0; q < Q; ++q) top[q].offer(acc[u][q], ids[u], alive(u, q), a.k);
                     }
+                };
+                if constexpr (carry_queue(MT)) {
+                    static_assert(CARRY_QWIDE * PRUNE_DEEPEN >= 32 * ILP * Q,
+                                  "a tile with more than CARRY_QWIDE survivors must have been deepened to SAX");
+                    if (total > CARRY_QWIDE) {
+                        finish_qwide();
+                    } else if (total > 0) {
+                        // Queue the survivors: first (partial sum, tile row | q << 24) while the sums are in
+                        // registers, then, entry per lane, each row's remaining sub-codes (dep .. 15 of its 16-byte
+                        // word) and its chunk-relative row from the stage slot, which keeps the sums' live range short.
+                        const unsigned lt = (1u << lane) - 1u;
+                        const int first = qcnt;
+#pragma unroll
+                        for (int u = 0; u < ILP; ++u)
+#pragma unroll
+                            for (int q = 0; q < Q; ++q) {
+                                const unsigned mk = __ballot_sync(FULL, alive(u, q));
+                                if (mk != 0) {  // uniform: most (row group, query) ballots are empty
+                                    if ((mk >> lane) & 1u)
+                                        reinterpret_cast<int2*>(my_carry + qcnt + __popc(mk & lt))[0] =
+                                            make_int2(__float_as_int(acc[u][q]), (u * 32 + lane) | (q << 24));
+                                    qcnt += __popc(mk);
+                                }
+                            }
+                        __syncwarp();
+                        const uint32_t dsel = (uint32_t)(dep - SA) / 2u;
+                        // the chunk's first window starts row_begin % 64 rows before it (windows are 64-aligned)
+                        const uint32_t tile_rel = (uint32_t)(row_begin & (PLACE_WINDOW - 1)) + (uint32_t)tile * (uint32_t)tile_rows;
+                        for (int e = first + lane; e < qcnt; e += 32) {
+                            uint32_t* ent = reinterpret_cast<uint32_t*>(my_carry + e);
+                            const uint32_t y = ent[1];
+                            const uint32_t r = y & 0xffffu;
+                            const uint2 zw = reinterpret_cast<const uint2*>(st + r)[1];  // bytes 8..15 of row r
+                            const uint32_t lo = dep == 8 ? zw.x : dep == 10 ? __funnelshift_r(zw.x, zw.y, 16) : zw.y;
+                            const uint32_t hi = dep == 8 ? zw.y : dep == 10 ? zw.y >> 16 : 0u;
+                            const uint32_t rel = ((tile_rel + r) & ~(uint32_t)(PLACE_WINDOW - 1)) + st_perm[r];
+                            reinterpret_cast<uint4*>(ent)[0] =
+                                make_uint4(ent[0], rel | (y & (7u << 24)) | (dsel << 27), lo, hi);
+                        }
+                    }
+                    __syncwarp();  // the stage slot is free: queued pairs carry their codes
+                    if (lane == 0) refill();
+                    carry_drain(false);
+                } else {
+                int cnt = 0;
+                if (2 * total > 32 * ILP * Q) {
+                    // Most pairs survive (no tight bound yet), which the deepening above leaves possible only at
+                    // dep == SAX: finishing every row with the Q-wide lookups of the full scan is cheaper than
+                    // finishing pairs one query per lane.
+                    finish_qwide();
                 } else {
                     const unsigned lt = (1u << lane) - 1u;
 #pragma unroll
                     for (int u = 0; u < ILP; ++u)
 #pragma unroll
                         for (int q = 0; q < Q; ++q) {
-                            if (masks[u][q] != 0) {  // uniform: most (row group, query) ballots are empty
-                                if ((masks[u][q] >> lane) & 1u)
-                                    my_queue[cnt + __popc(masks[u][q] & lt)] =
+                            const unsigned mk = __ballot_sync(FULL, alive(u, q));
+                            if (mk != 0) {  // uniform: most (row group, query) ballots are empty
+                                if ((mk >> lane) & 1u)
+                                    my_queue[cnt + __popc(mk & lt)] =
                                         make_int2(__float_as_int(acc[u][q]), (u * 32 + lane) | (q << 16));
-                                cnt += __popc(masks[u][q]);
+                                cnt += __popc(mk);
                             }
                         }
                 }
@@ -526,6 +647,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                 }
                 __syncwarp();  // the queue and the stage slot are free again
                 if (lane == 0) refill();
+                }
                 // Publish improved list thresholds as global bounds for the other warps and blocks.
 #pragma unroll
                 for (int q = 0; q < Q; ++q) {
@@ -535,6 +657,10 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                     }
                 }
             }
+        }
+        if constexpr (PRUNE && carry_queue(MT)) {
+            if (!warp_abort) carry_drain(true);  // queued pairs of the item's last tiles
+            qcnt = 0;
         }
         if (warp_abort && lane == 0) {
             // Let this warp's copies still in flight land before the block can exit.

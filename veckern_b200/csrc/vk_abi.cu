@@ -275,6 +275,9 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     int64_t chunks = lo;
     if (t.blocks_per_query > 0) {
         chunks = std::min<int64_t>(t.blocks_per_query, max_chunks);
+        // the pruned m = 16 scan addresses a chunk's rows in 24 bits of its queue entries
+        if (p.prune && vk::carry_queue(ix->m))
+            chunks = std::max<int64_t>(chunks, ceil_div(ix->n_pad, vk::CARRY_MAX_CHUNK_ROWS));
     } else {
         double best = 1e300;
         for (int64_t c = lo; c <= hi; ++c) {
