@@ -172,7 +172,10 @@ class ClockSampler:
 # (config, rows scanned per GPU, m, nq, k); a run whose shard matches no capture reports the bytes scaled from the
 # capture of the same config by rows (codes and placement bytes grow with rows, LUT bytes with nq), marked scaled.
 NCU_TRAFFIC = {
-    ("c1", 1_000_000, 16, 1000, 10): {"dram_bytes_per_launch": 33_660_416, "kernel": "scan_kernel<8,16,2,1,16,1>"},
+    ("c1", 1_000_000, 16, 1000, 10): {"dram_bytes_per_launch": 33_659_136, "kernel": "scan_kernel<8,16,2,1,16,1>"},
+    ("c3", 10_000_000, 16, 1000, 10): {"dram_bytes_per_launch": 196_180_000, "kernel": "scan_kernel<8,16,2,1,16,1>"},
+    # ncu prints this capture in GB with two decimals
+    ("c3", 100_000_000, 16, 10_000, 10): {"dram_bytes_per_launch": 18_047_000_000, "kernel": "scan_kernel<8,16,2,1,16,1>"},
 }
 
 
