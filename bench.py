@@ -50,9 +50,14 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample duration")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--skip-full", action="store_true", help="skip the full-scan (early_abandon=0) comparison loops")
+    p.add_argument("--skip-h16", action="store_true", help="skip the half-precision LUT (lut_f16) loops")
+    p.add_argument("--ivf-nprobe", type=int, default=16,
+                   help="one GPU, configs 0-2: also an IVF search with 256 lists probing this many (0: skip)")
     p.add_argument("--no-verify", action="store_true",
                    help="N > 1: skip rank 0's search of the whole database on its GPU, which checks the merged results "
                         "bit-exactly (done by default)")
+    p.add_argument("--no-coop", action="store_true",
+                   help="N > 1: shards prune with their own bounds only (no bound exchange between the GPUs)")
     p.add_argument("--sharded", default="c3",
                    help="generated configuration (c3 or c4) also measured sharded by id over the run's GPUs, reported "
                         "under 'sharded'; 'none' to skip")
@@ -403,6 +408,44 @@ def wavefront_floor(codes_sample: np.ndarray, perm: np.ndarray, Q: int, lookups:
     return wf, wf_rows, floor_ms
 
 
+class ShardExchange:
+    """This rank's side of a cooperative sharded search (N > 1 unless --no-coop): the shards' scans lower each
+    other's pruning bounds with posted atomics over NVLink (vk_search_device_coop), exchange arrays mapped across
+    the rank processes with CUDA IPC handles (all-gathered once). Every rank calls search() in the same order, so
+    the epochs agree. close() only after all ranks have synchronised: no rank's kernel may still write into this
+    rank's memory."""
+
+    def __init__(self, args, world: int, local: int, nq: int):
+        self.coop = None
+        self.active = False
+        self.epoch = 0
+        if world > 1 and not args.no_coop:
+            import torch.distributed as dist
+
+            from veckern_b200 import CoopSearch, VkError
+            self.coop = CoopSearch(local, nq)
+            handles = [None] * world
+            dist.all_gather_object(handles, self.coop.ipc_handle())
+            try:
+                self.coop.attach_ipc(handles)
+                self.active = True
+            except VkError as e:  # e.g. GPUs without a link that carries atomics: search this shard alone
+                print(f"bound exchange unavailable: {e}", file=sys.stderr, flush=True)
+
+    def search(self, s, d_q, k, d_out, stream, tuning=None):
+        if not self.active:
+            s.search_device(d_q, k, d_out, stream, tuning=tuning)
+        else:
+            self.epoch += 1
+            s.search_device_coop(self.coop, self.epoch, d_q, k, d_out, stream, tuning=tuning)
+
+    def close(self):
+        if self.coop is not None:
+            self.coop.close()
+            self.coop = None
+            self.active = False
+
+
 def run_sharded(args, rank: int, world: int, local: int, stream, flush):
     """A generated configuration (default c3: 100M rows, m 16, nq 10,000, k 10) sharded contiguously by id over the
     run's ranks, each shard's codes generated on its GPU: every rank searches its shard, the per-shard top-k lists are
@@ -427,6 +470,7 @@ def run_sharded(args, rank: int, world: int, local: int, stream, flush):
     d_local = torch.empty((nq, k), dtype=torch.int64, device="cuda")
     d_gather = torch.empty((world, nq, k), dtype=torch.int64, device="cuda") if world > 1 else None
     d_final = torch.empty((nq, k), dtype=torch.int64, device="cuda") if world > 1 else d_local
+    shx = ShardExchange(args, world, local, nq)
 
     def exchange():
         def merge(buf, lay):
@@ -435,7 +479,7 @@ def run_sharded(args, rank: int, world: int, local: int, stream, flush):
         gather_and_merge(d_local, d_gather, nq, k, lambda buf, x: dist.all_gather_into_tensor(buf, x), merge)
 
     for _ in range(args.sharded_warmup):
-        s.search_device(d_q, k, d_local, stream)
+        shx.search(s, d_q, k, d_local, stream)
         if world > 1:
             exchange()
     s.sync(stream)
@@ -449,7 +493,7 @@ def run_sharded(args, rank: int, world: int, local: int, stream, flush):
     for e in evs:
         flush.zero_()
         e[0].record(stream)
-        s.search_device(d_q, k, d_local, stream)
+        shx.search(s, d_q, k, d_local, stream)
         e[1].record(stream)
         if world > 1:
             exchange()
@@ -503,12 +547,68 @@ def run_sharded(args, rank: int, world: int, local: int, stream, flush):
                                         "list merge)"},
                "hbm": {"code_bytes_per_gpu": int(sh.rows * m),
                        "traffic": ncu_traffic(name, sh.rows, m, nq, k), "peak_gbs_measured": _peak("hbm_gbs")},
+               "bound_exchange": shx.active,
                "verified_against_single_gpu": verified, "clocks": clk,
                "l2": "flushed (256 MB write) before every timed step"}
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()  # no rank's scan may still write into this rank's exchange array
+    shx.close()
     s.close()
     del d_q, d_local, d_gather, d_final
     torch.cuda.empty_cache()
     return out
+
+
+def run_ivf(args, w, spec, exact_ids, stream, flush, local):
+    """IVF search over the same database (one GPU): 256 lists whose coarse centroids are trained by the device PQ
+    trainer with m = 1 (the reference's Lloyd iterations over whole vectors) on the configuration's training
+    sample, rows assigned to the nearest; each query probes --ivf-nprobe lists. Device-resident steps timed like
+    the headline; recall = share of the exact flat search's top-k ids it returns."""
+    import torch
+
+    from veckern_b200 import IVFSearcher, Tuning, assign_lists, data, device_result_split
+    n, d, nq, k = spec["n"], spec["d"], spec["nq"], spec["k"]
+    t0 = time.perf_counter()
+    train = data.gen_mixture(spec["mix_seed"], spec["mix_seed"], min(spec.get("train_rows", n), n), d) \
+        if spec["kind"] == "mixture" else data.gen_normal(spec["data_seed"], min(n, 100_000), d)
+    coarse = data.pq_train_gpu(train, 1, 10, spec.get("pq_seed", 1)).reshape(256, d)
+    lists = np.empty(n, np.int32)
+    step = 1 << 20
+    for a in range(0, n, step):
+        b = min(n, a + step)
+        x = data.gen_mixture(spec["mix_seed"], spec["mix_seed"], b - a, d, row0=a) if spec["kind"] == "mixture" \
+            else data.gen_normal(spec["data_seed"], b - a, d, row0=a)
+        lists[a:b] = assign_lists(x, coarse, local)
+    nprobe = args.ivf_nprobe
+    with IVFSearcher(w.centroids, w.codes, coarse, lists, device=local) as ivf:
+        build_s = time.perf_counter() - t0
+        ivf.set_tuning(Tuning(queries_per_block=args.qpb, vectors_per_step=args.ilp))
+        d_q = torch.from_numpy(w.queries).cuda()
+        out = torch.empty((nq, k), dtype=torch.int64, device="cuda")
+        for _ in range(args.warmup):
+            ivf.search_device(d_q, k, nprobe, out, stream)
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for e in ev:
+            flush.zero_()
+            e[0].record(stream)
+            ivf.search_device(d_q, k, nprobe, out, stream)
+            e[1].record(stream)
+        torch.cuda.synchronize()
+        ivf.sync(stream)
+        ms = sum(a.elapsed_time(b) for a, b in ev) / max(1, args.steps)
+        ids = device_result_split(out)[1].cpu().numpy()
+    ids_x = device_result_split(exact_ids)[1].cpu().numpy()
+    recall = float(np.mean([len(set(a) & set(b)) / k for a, b in zip(ids, ids_x)]))
+    sizes = np.bincount(lists, minlength=256)
+    return {"value": round(nq / (ms / 1e3), 1), "unit": "queries/s", "ms_per_step": round(ms, 4), "nlist": 256,
+            "nprobe": nprobe, "recall_vs_flat": round(recall, 5),
+            "list_rows": {"min": int(sizes.min()), "median": int(np.median(sizes)), "max": int(sizes.max())},
+            "build_s": round(build_s, 2),
+            "note": "IVF search (vk_ivf_*): the flat search restricted to the rows of each query's nprobe nearest "
+                    "lists, bit-exact against its CPU restatement; recall_vs_flat = share of the exact flat "
+                    "search's top-k ids it returns"}
 
 
 def run_ours(args):
@@ -540,6 +640,7 @@ def run_ours(args):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
 
     from veckern_b200.shard import gather_and_merge
+    shx = ShardExchange(args, world, local, nq)
 
     def exchange():
         """One all-gather of the per-shard lists over NCCL, then the GPU merge into d_final."""
@@ -549,7 +650,7 @@ def run_ours(args):
         gather_and_merge(d_local, d_gather, nq, k, lambda buf, x: dist.all_gather_into_tensor(buf, x), merge)
 
     def step_device(tun=None):
-        s.search_device(d_q, k, d_local, stream, tuning=tun)
+        shx.search(s, d_q, k, d_local, stream, tuning=tun)
         if world > 1:
             exchange()
 
@@ -575,6 +676,7 @@ def run_ours(args):
         dist.barrier()
     s.sync(stream)
     dev_ms = sum(a.elapsed_time(b) for a, b in ev)
+    exact_ids = (d_final if world > 1 else d_local).clone()
 
     # ---- the same steps with early abandoning off (full scan of every (query, row, sub-space) lookup)
     full_tuning = Tuning(queries_per_block=args.qpb, vectors_per_step=args.ilp, blocks_per_query=args.bpq,
@@ -593,46 +695,91 @@ def run_ours(args):
     s.sync(stream)
     full_ms = float("nan") if args.skip_full else sum(a.elapsed_time(b) for a, b in ev_full)
 
-    # ---- e2e: the host-buffer C-ABI call (vk_search), rank-local; N > 1 adds gather + merge + result copy
-    h_q = torch.from_numpy(w.queries).pin_memory().numpy()
+    # ---- the same steps with half-precision LUTs (VK_LUT_F16: approximate, exactly defined; recall reported)
+    h16_tuning = Tuning(queries_per_block=args.qpb, vectors_per_step=args.ilp, blocks_per_query=args.bpq,
+                        lut_f16=True)
+    h16_ok = m in (16, 32, 64) and not args.skip_h16
+    for _ in range(args.warmup if h16_ok else 0):
+        step_device(h16_tuning)
+    torch.cuda.synchronize()
+    ev_h16 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    for i in range(args.steps if h16_ok else 0):
+        flush.zero_()
+        ev_h16[i][0].record(stream)
+        step_device(h16_tuning)
+        ev_h16[i][1].record(stream)
+    torch.cuda.synchronize()
+    s.sync(stream)
+    h16_ms = sum(a.elapsed_time(b) for a, b in ev_h16) if h16_ok else float("nan")
+    h16_ids = (d_final if world > 1 else d_local).clone() if h16_ok else None
+
+    # ---- e2e. N = 1: the host-buffer C-ABI call (vk_search: H2D, LUT, scan, merge, D2H), its stage events giving
+    # the scan kernel's time. N > 1: the pinned host queries copied to the device, this rank's shard search (with
+    # the bound exchange), the all-gather + merge, and the merged result copied back to pinned host memory.
+    h_q_t = torch.from_numpy(w.queries).pin_memory()
+    h_q = h_q_t.numpy()
     from veckern_b200 import NEIGHBOR_DTYPE
     h_out = torch.empty((nq, k), dtype=torch.int64).pin_memory().numpy().view(NEIGHBOR_DTYPE)
     h_final = torch.empty((nq, k), dtype=torch.int64).pin_memory()
+    d_q2 = torch.empty_like(d_q)
     e2e_ms, scan_ms, lut_ms, sel_ms = [], [], [], []
     for i in range(args.warmup + args.steps):
         flush.zero_()
         torch.cuda.synchronize()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        _, t = s.search(h_q, k, out=h_out)  # synchronous: H2D, LUT, scan, merge, D2H
-        if world > 1:
-            d_local.copy_(torch.from_numpy(h_out.view(np.int64)), non_blocking=True)
+        if world == 1:
+            t0.record(stream)
+            _, t = s.search(h_q, k, out=h_out)  # synchronous: H2D, LUT, scan, merge, D2H
+            t1.record(stream)
+        else:
+            ta = torch.cuda.Event(enable_timing=True)
+            tb = torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            d_q2.copy_(h_q_t, non_blocking=True)
+            ta.record(stream)
+            shx.search(s, d_q2, k, d_local, stream)
+            tb.record(stream)
             exchange()
             h_final.copy_(d_final, non_blocking=True)
-        t1.record(stream)
+            t1.record(stream)
         torch.cuda.synchronize()
         total = t0.elapsed_time(t1)
         if i >= args.warmup:
             e2e_ms.append(total)
-            scan_ms.append(t.scan_ms)
-            lut_ms.append(t.lut_ms)
-            sel_ms.append(t.select_ms)
-    # scan-kernel duration of the full scan, from the same stage events
+            if world == 1:
+                scan_ms.append(t.scan_ms)
+                lut_ms.append(t.lut_ms)
+                sel_ms.append(t.select_ms)
+            else:  # LUT + scan + merge of the shard: its scan dominates
+                scan_ms.append(ta.elapsed_time(tb))
+                lut_ms.append(float("nan"))
+                sel_ms.append(float("nan"))
+    # scan-kernel duration of the full scan, from the same stage events (one GPU)
     s.set_tuning(full_tuning)
-    full_scan_ms = [float("nan")] if args.skip_full else []
-    for i in range(0 if args.skip_full else args.warmup + args.steps):
+    full_scan_ms = [float("nan")] if args.skip_full or world > 1 else []
+    for i in range(0 if args.skip_full or world > 1 else args.warmup + args.steps):
         flush.zero_()
         _, t = s.search(h_q, k, out=h_out)
         if i >= args.warmup:
             full_scan_ms.append(t.scan_ms)
+    h16_scan_ms = [float("nan")]
+    if h16_ok and world == 1:
+        s.set_tuning(h16_tuning)
+        h16_scan_ms = []
+        for i in range(args.warmup + args.steps):
+            flush.zero_()
+            _, t = s.search(h_q, k, out=h_out)
+            if i >= args.warmup:
+                h16_scan_ms.append(t.scan_ms)
     s.set_tuning(tuning)
     clk = clocks.stop()
 
     verified = None
     if not args.no_verify and world > 1:
         # the gathered + merged result of the last device step against one GPU over the whole database
-        s.search_device(d_q, k, d_local, stream)
+        shx.search(s, d_q, k, d_local, stream)
         exchange()
         torch.cuda.synchronize()
         if rank == 0:
@@ -652,10 +799,25 @@ def run_ours(args):
         dist.barrier()
 
     dev_ms_t = torch.tensor([dev_ms, float(np.sum(e2e_ms)), float(np.mean(scan_ms)), full_ms,
-                             float(np.mean(full_scan_ms))], device="cuda")
+                             float(np.mean(full_scan_ms)), h16_ms, float(np.mean(h16_scan_ms))], device="cuda")
     if world > 1:
         dist.all_reduce(dev_ms_t, op=dist.ReduceOp.MAX)
-    dev_ms, e2e_total, scan_mean, full_ms, full_scan_mean = dev_ms_t.tolist()
+    dev_ms, e2e_total, scan_mean, full_ms, full_scan_mean, h16_ms, h16_scan_mean = dev_ms_t.tolist()
+    h16_block = None
+    ivf_block = None
+    if world == 1 and args.ivf_nprobe > 0 and spec["kind"] in ("mixture", "normal") and m in (16, 32):
+        ivf_block = run_ivf(args, w, spec, exact_ids, stream, flush, local)
+    if h16_ok and rank == 0:
+        from veckern_b200 import device_result_split
+        ids_h = device_result_split(h16_ids)[1].cpu().numpy()
+        ids_x = device_result_split(exact_ids)[1].cpu().numpy()
+        recall = float(np.mean([len(set(a) & set(b)) / k for a, b in zip(ids_h, ids_x)]))
+        h16_block = {"value": round(nq / (h16_ms / args.steps / 1e3), 1), "unit": "queries/s",
+                     "ms_per_step": round(h16_ms / args.steps, 4), "scan_kernel_ms": round(h16_scan_mean, 4),
+                     "recall_vs_fp32": round(recall, 5),
+                     "note": "half-precision LUTs (lut_precision = VK_LUT_F16): per-query power-of-two scale, "
+                             "entries rounded to half, fp32 sums; bit-exact against its CPU restatement; "
+                             "recall_vs_fp32 = share of the exact search's top-k ids it returns"}
 
     if rank == 0:
         ms_step = dev_ms / args.steps
@@ -697,6 +859,11 @@ def run_ours(args):
             "hbm": {"code_bytes_per_launch": int((hi - lo) * m), "peak_gbs_measured": _peak("hbm_gbs")},
         }
         cpu = None if args.no_cpu_baseline else cpu_baseline(args, w, spec)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()  # no rank's scan may still write into this rank's exchange array
+    bound_exchange = shx.active
+    shx.close()
     sharded = None
     if args.sharded not in ("none", args.config):
         s.close()
@@ -710,11 +877,14 @@ def run_ours(args):
             "config": {"workload": workload_name(spec, args.config), "n": n, "d": spec["d"], "m": m, "nq": nq,
                        "k": k, "queries_per_block": Q, "vectors_per_step": s.last_launch().vectors_per_step,
                        "shards": world, "l2": "flushed (256 MB write) before every timed step",
+                       "bound_exchange": bound_exchange,
                        "parallelism": f"id-sharded x{world}" if world > 1 else "single GPU"},
             "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
                     "h2d_bytes_per_step": int(w.queries.nbytes), "d2h_bytes_per_step": int(nq * k * 8),
                     "stages_ms": {"lut": round(float(np.mean(lut_ms)), 4), "scan": round(scan_mean, 4),
                                   "select": round(float(np.mean(sel_ms)), 4)}},
+            "lut_f16": h16_block,
+            "ivf": ivf_block,
             "full_scan": {"value": round(nq / (full_ms / args.steps / 1e3), 1), "unit": "queries/s",
                           "ms_per_step": round(full_ms / args.steps, 4), "scan_kernel_ms": round(full_scan_mean, 4),
                           "note": "early abandoning off: every (query, row, sub-space) lookup executed"},

@@ -62,18 +62,31 @@ typedef struct {
     int clock_mhz;              /* max SM clock */
 } vk_device_info_t;
 
+/* LUT precision of a search (vk_tuning_t.lut_precision). */
+enum {
+    VK_LUT_F32 = 0, /* fp32 entries: results bit-identical to the reference CPU path (the default) */
+    VK_LUT_F16 = 1  /* half entries, summed in fp32: an approximate search with its own exact definition (below) */
+};
+
 /* Replaces gpu::Tuning (include/veckern/gpu.hpp:29-34) with the same meaning and the same accepted values
  * (src/cuda/searcher.cu:450-460): scan_threads multiple of 32 in [32, 1024] (used by distances()),
  * blocks_per_query >= 0 (vector chunks per query group; 0 = auto), queries_per_block in {1, 2, 4, 8},
- * vectors_per_step in {1, 2, 4} (32-vector groups each warp holds in flight). Added field:
+ * vectors_per_step in {1, 2, 4} (32-vector groups each warp holds in flight). Added fields:
  * early_abandon (1 = default, 0 = off): stop summing a (query, row) pair once its partial distance exceeds a
- * proven bound on the query's k-th distance (m in {16, 32, 64}); results are identical either way. */
+ * proven bound on the query's k-th distance (m in {16, 32, 64}); results are identical either way.
+ * lut_precision: VK_LUT_F32 (default) or VK_LUT_F16, the half-precision lookup tables the reference lists as a
+ * next step (README.md:219), for m in {16, 32, 64}, with 4 or 8 queries per block. Per query, T[s][c] is the fp32
+ * entry of the exact path, M its largest value, e = 15 - E where M = f * 2^E with f in [0.5, 1) (clamped to
+ * [-64, 64]; e = 0 when M = 0); the table holds half(T * 2^e) rounded to nearest even; a row's distance is the
+ * fp32 sum of its entries in sub-space order times 2^-e, and the k smallest (distance, id) pairs are returned.
+ * oracle/vk_oracle.c restates this definition on the CPU (vko_adc_search_h16). vk_distances always uses fp32. */
 typedef struct {
     int scan_threads;
     int blocks_per_query;
     int queries_per_block;
     int vectors_per_step;
     int early_abandon;
+    int lut_precision;
 } vk_tuning_t;
 
 /* Replaces gpu::Timings (include/veckern/gpu.hpp:46-50): milliseconds per stage from CUDA events. */
@@ -174,6 +187,34 @@ int vk_search_device(vk_index_t* index, const float* d_queries, int64_t nq, int 
 /* Waits for the index's work on `stream` (NULL = the default stream) and reports any kernel-side error. */
 int vk_index_sync(vk_index_t* index, void* stream);
 
+/* Cooperative sharded search (no counterpart in the reference, which runs on one device). The shards of one
+ * database (one index per GPU, ids offset by id_base) searched with the same queries share, while they scan, each
+ * query's pruning bound: every shard's scan lowers the other shards' bounds with posted atomics into their memory
+ * (over NVLink) and reads its own, so a small shard prunes with the bound of the whole database instead of its own.
+ * A shard's lists then hold every pair of that shard that belongs to the merged top-k, and may miss others (padded
+ * with {+inf, -1}): merge the shards' lists (vk_merge_topk_device) for the exact result, which equals one index
+ * over all rows. Pairs are exchanged as (epoch, bound): all shards of a search pass the same epoch, and each new
+ * search a larger one (>= 1); bounds of an older epoch are ignored. A shard's memory must outlive every search of
+ * the others that uses it: synchronise all shards (e.g. a barrier after the last search) before destroying any.
+ *   vk_coop_create      exchange array of nq_max queries on `device`
+ *   vk_coop_ipc_handle  its VK_COOP_HANDLE_BYTES-byte handle (CUDA IPC handle, length, device), for shards in
+ *                       other processes of this node
+ *   vk_coop_attach_ipc  maps the other shards' arrays from their handles (the list may include its own)
+ *   vk_coop_attach      the same for shards in this process (the list may include itself)
+ * Shards on different GPUs need a link that carries atomics (NVLink); attaching fails with VK_ERR_UNSUPPORTED
+ * otherwise. A search's nq may not exceed any attached shard's nq_max. */
+#define VK_COOP_HANDLE_BYTES 80
+typedef struct vk_coop vk_coop_t;
+int vk_coop_create(int device, int64_t nq_max, vk_coop_t** out);
+int vk_coop_ipc_handle(const vk_coop_t* coop, void* handle);
+int vk_coop_attach_ipc(vk_coop_t* coop, int n, const void* handles);
+int vk_coop_attach(vk_coop_t* coop, int n, vk_coop_t* const* coops);
+int vk_coop_destroy(vk_coop_t* coop);
+/* vk_search_device for one shard of a cooperative search (the pruned scan; with early_abandon = 0 the shard
+ * neither reads nor lowers shared bounds). */
+int vk_search_device_coop(vk_index_t* index, vk_coop_t* coop, uint32_t epoch, const float* d_queries, int64_t nq,
+                          int k, const vk_tuning_t* tuning, vk_neighbor_t* d_out, void* stream);
+
 /* Replaces PQSearcher::distances (src/cuda/searcher.cu:522-547): the full nq x n ADC matrix to HOST memory.
  * Rejected for the fused variants, as in the reference. */
 int vk_distances(vk_index_t* index, const float* queries, int64_t nq, int variant, const vk_tuning_t* tuning,
@@ -213,6 +254,34 @@ int vk_pq_train_device(int device, const float* d_x, int64_t n, int d, int m, in
  * the same integers as vk_gen_codes_host. */
 int vk_gen_codes_device(int device, uint64_t seed, const uint32_t* cdf, int clusters, int m, int64_t row_first,
                         int64_t n, uint8_t* d_codes, void* stream);
+
+/* IVF (inverted-file) search: the IVF partitioning the reference lists as a next step (README.md:219). Rows are
+ * partitioned into nlist lists (list_of[i] in [0, nlist), e.g. the nearest of nlist coarse centroids:
+ * vk_ivf_assign_device; vk_pq_train_device with m = 1 trains 256 such centroids); a search scans only the rows of
+ * each query's nprobe nearest lists. Definition (restated on the CPU by oracle vko_ivf_search): the probed lists are
+ * the nprobe smallest (l2sq(query, coarse[l]), l) pairs (the reference's exact l2sq over all d dimensions, ties to
+ * the lower list), and the result is the k smallest (distance, id) pairs among their rows, distances being the flat
+ * search's (the same fp32 LUT summed in sub-space order): the flat search restricted to those rows, bit for bit.
+ * PQ codes are not residuals, so one LUT per query serves every list. m = 16 or 32, fp32 LUTs, 1 <= k <= 128,
+ * 1 <= nprobe <= min(128, nlist); a query whose lists hold fewer than k rows is padded with {+inf, -1}.
+ *   vk_ivf_create          builds the index from HOST centroids, codes (n x m, row-major), coarse centroids
+ *                          (nlist x d) and list_of (n)
+ *   vk_ivf_search          HOST queries and results, synchronous (timings: transfer_ms and, in scan_ms, the
+ *                          whole device search)
+ *   vk_ivf_search_device   DEVICE queries and results on `stream`, asynchronous (vk_ivf_sync reads the status)
+ *   vk_ivf_assign_device   nearest coarse centroid of each DEVICE row (exact l2sq, first minimum wins) */
+typedef struct vk_ivf vk_ivf_t;
+int vk_ivf_create(int device, const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
+                  const float* coarse, int nlist, const int32_t* list_of, vk_ivf_t** out);
+int vk_ivf_destroy(vk_ivf_t* ivf);
+int vk_ivf_info(const vk_ivf_t* ivf, int64_t* n, int* nlist, int64_t* slots);
+int vk_ivf_search(vk_ivf_t* ivf, const float* queries, int64_t nq, int k, int nprobe, const vk_tuning_t* tuning,
+                  vk_neighbor_t* out, vk_timings_t* timings);
+int vk_ivf_search_device(vk_ivf_t* ivf, const float* d_queries, int64_t nq, int k, int nprobe,
+                         const vk_tuning_t* tuning, vk_neighbor_t* d_out, void* stream);
+int vk_ivf_sync(vk_ivf_t* ivf, void* stream);
+int vk_ivf_assign_device(int device, const float* d_x, int64_t n, int d, const float* d_coarse, int nlist,
+                         int32_t* d_list_of, void* stream);
 
 /* No counterpart in the reference. A device-resident search that allocates nothing, for callers that must not
  * call cudaMalloc or cudaFree: code running where an allocation would synchronise the device and stall other

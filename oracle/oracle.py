@@ -47,6 +47,12 @@ class Port:
         L.vko_rerank_exact.argtypes = [_f32p, C.c_int, _f32p, _i64, _i32p, C.c_int, C.c_int, _f32p, _i32p]
         L.vko_recall_at_k.argtypes = [_i32p, _i64, _i32p, _i64, _i64, C.c_int]
         L.vko_recall_at_k.restype = C.c_double
+        L.vko_compute_lut_h16.argtypes = [_f32p, C.c_int, C.c_int, _f32p, _i64, _f32p,
+                                          np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")]
+        L.vko_adc_search_h16.argtypes = [_f32p, C.c_int, C.c_int, _u8p, _i64, _f32p, _i64, C.c_int, _f32p, _i32p,
+                                         C.c_int]
+        L.vko_ivf_search.argtypes = [_f32p, C.c_int, C.c_int, _u8p, _i32p, _i64, _f32p, C.c_int, _f32p, _i64,
+                                     C.c_int, C.c_int, _f32p, _i32p, _i32p, C.c_int]
         L.vko_stream_create.argtypes = [_f32p, _i64, C.c_int, C.c_int]
         L.vko_stream_create.restype = C.c_void_p
         L.vko_stream_feed.argtypes = [C.c_void_p, _u8p, _i64, _i64, C.c_int]
@@ -88,6 +94,45 @@ class Port:
         i = np.empty((nq, k), np.int32)
         self.lib.vko_adc_search(centroids, m, dsub, codes, codes.shape[0], queries, nq, k, d, i, threads)
         return d, i
+
+    def compute_lut_h16(self, centroids, queries):
+        """(tables [nq, m, 256]: the half-rounded, scaled entries as float32, exponents [nq] int32) of the
+        half-precision LUT search."""
+        centroids = _f32(centroids)
+        m, ksub, dsub = centroids.shape
+        queries = _f32(queries).reshape(-1, m * dsub)
+        lut = np.empty((queries.shape[0], m, 256), np.float32)
+        exps = np.empty(queries.shape[0], np.int32)
+        self.lib.vko_compute_lut_h16(centroids, m, dsub, queries, queries.shape[0], lut, exps)
+        return lut, exps
+
+    def adc_search_h16(self, centroids, codes, queries, k, threads=0):
+        """The half-precision LUT search (VK_LUT_F16 definition) -> (dists [nq, k], ids [nq, k])."""
+        centroids = _f32(centroids)
+        m, _, dsub = centroids.shape
+        codes = _u8(codes)
+        queries = _f32(queries).reshape(-1, m * dsub)
+        nq = queries.shape[0]
+        d = np.empty((nq, k), np.float32)
+        i = np.empty((nq, k), np.int32)
+        self.lib.vko_adc_search_h16(centroids, m, dsub, codes, codes.shape[0], queries, nq, k, d, i, threads)
+        return d, i
+
+    def ivf_search(self, centroids, codes, list_of, coarse, queries, nprobe, k, threads=0):
+        """IVF search (flat search over the rows of each query's nprobe nearest lists) -> (dists, ids, probes)."""
+        centroids = _f32(centroids)
+        m, _, dsub = centroids.shape
+        codes = _u8(codes)
+        list_of = np.ascontiguousarray(list_of, np.int32)
+        coarse = _f32(coarse)
+        queries = _f32(queries).reshape(-1, m * dsub)
+        nq = queries.shape[0]
+        d = np.empty((nq, k), np.float32)
+        i = np.empty((nq, k), np.int32)
+        probes = np.empty((nq, nprobe), np.int32)
+        self.lib.vko_ivf_search(centroids, m, dsub, codes, list_of, codes.shape[0], coarse, coarse.shape[0], queries,
+                                nq, nprobe, k, d, i, probes, threads)
+        return d, i, probes
 
     def topk_push_all(self, dists, ids, k):
         dists = _f32(dists)

@@ -176,6 +176,139 @@ void vko_adc_search(const float* centroids, int m, int dsub, const uint8_t* code
     }
 }
 
+/* ---------------------------------------------------------------- half-precision LUT search
+ * Not in the reference, which lists fp16 lookup tables as a next step (README.md:219); this is the definition the
+ * library's VK_LUT_F16 search implements (include/vk_abi.h, lut_precision), restated on the CPU:
+ *   T = the fp32 LUT of compute_lut; M = max over (s, c) of T; e = 15 - E with M = f * 2^E, f in [0.5, 1),
+ *   clamped to [-64, 64] (e = 0 when M = 0, 64 when M is subnormal); entry = half(T * 2^e), round to nearest even;
+ *   distance = (fp32 sum over s = 0..m-1 of the entries, from 0, in order) * 2^-e; top-k by (distance, id). */
+static int h16_exponent(float max) {
+    uint32_t bits;
+    memcpy(&bits, &max, sizeof(bits));
+    const int ef = (int)((bits >> 23) & 0xffu);
+    if (bits == 0u || ef == 255) return 0;
+    if (ef == 0) return 64;
+    const int e = 15 - (ef - 126);
+    return e < -64 ? -64 : e > 64 ? 64 : e;
+}
+
+/* x (>= 0, < 65520) rounded to the nearest half-precision value (ties to even), returned as a float. The step
+ * between halves around x is 2^(E - 10) for x in [2^E, 2^(E+1)), E >= -14, and 2^-24 below 2^-14 (subnormals);
+ * x / step is exact in double, so rounding it to an integer (nearbyint: ties to even) rounds x. */
+static float half_round(float x) {
+    if (x == 0.f) return x;
+    int ex;
+    frexp((double)x, &ex); /* x = f * 2^ex, f in [0.5, 1): x in [2^(ex-1), 2^ex) */
+    int E = ex - 1;
+    if (E < -14) E = -14;
+    const double step = ldexp(1.0, E - 10);
+    return (float)(nearbyint((double)x / step) * step);
+}
+
+void vko_compute_lut_h16(const float* centroids, int m, int dsub, const float* queries, int64_t nq, float* lut,
+                         int* exps) {
+    vko_compute_lut(centroids, m, dsub, queries, nq, lut);
+#pragma omp parallel for schedule(static)
+    for (int64_t q = 0; q < nq; ++q) {
+        float* t = lut + q * m * KSUB;
+        float mx = 0.f;
+        for (int j = 0; j < m * KSUB; ++j) mx = t[j] > mx ? t[j] : mx;
+        const int e = h16_exponent(mx);
+        for (int j = 0; j < m * KSUB; ++j) t[j] = half_round(ldexpf(t[j], e));
+        exps[q] = e;
+    }
+}
+
+void vko_adc_search_h16(const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
+                        const float* queries, int64_t nq, int k, float* out_d, int32_t* out_i, int threads) {
+#ifdef _OPENMP
+    const int nt = threads > 0 ? threads : omp_get_max_threads();
+#else
+    const int nt = 1;
+    (void)threads;
+#endif
+    const int64_t d = (int64_t)m * dsub;
+#pragma omp parallel num_threads(nt)
+    {
+        float* lut = (float*)malloc(sizeof(float) * (size_t)m * KSUB);
+        float* hd = (float*)malloc(sizeof(float) * (size_t)(k > 0 ? k : 1));
+        int32_t* hi = (int32_t*)malloc(sizeof(int32_t) * (size_t)(k > 0 ? k : 1));
+#pragma omp for schedule(dynamic)
+        for (int64_t q = 0; q < nq; ++q) {
+            vko_compute_lut(centroids, m, dsub, queries + q * d, 1, lut);
+            float mx = 0.f;
+            for (int j = 0; j < m * KSUB; ++j) mx = lut[j] > mx ? lut[j] : mx;
+            const int e = h16_exponent(mx);
+            for (int j = 0; j < m * KSUB; ++j) lut[j] = half_round(ldexpf(lut[j], e));
+            topk_t t;
+            topk_init(&t, k, hd, hi);
+            for (int64_t i = 0; i < n; ++i) topk_push(&t, ldexpf(adc_one(lut, codes + i * m, m), -e), (int32_t)i);
+            topk_write(&t, out_d + q * k, out_i + q * k);
+        }
+        free(lut);
+        free(hd);
+        free(hi);
+    }
+}
+
+/* ---------------------------------------------------------------- IVF (inverted-file) search
+ * Not in the reference, which lists IVF partitioning as a next step (README.md:219); this is the definition the
+ * library's IVF search implements, restated on the CPU. Rows belong to lists (list_of[i] in [0, nlist)); per query:
+ *   probes = the nprobe smallest (l2sq(query, coarse[l]), l) pairs over the lists (the exact l2sq of
+ *            common.hpp:27-34 over all d dimensions; ties to the lower list);
+ *   result = the k smallest (ADC distance, row) pairs over the rows of the probed lists, the ADC distance being the
+ *            flat search's (the same fp32 LUT, summed in sub-space order): the flat search restricted to those rows.
+ * probes_out (optional, nq x nprobe): the probed lists in ascending (distance, list) order. */
+void vko_ivf_search(const float* centroids, int m, int dsub, const uint8_t* codes, const int32_t* list_of, int64_t n,
+                    const float* coarse, int nlist, const float* queries, int64_t nq, int nprobe, int k,
+                    float* out_d, int32_t* out_i, int32_t* probes_out, int threads) {
+#ifdef _OPENMP
+    const int nt = threads > 0 ? threads : omp_get_max_threads();
+#else
+    const int nt = 1;
+    (void)threads;
+#endif
+    const int64_t d = (int64_t)m * dsub;
+#pragma omp parallel num_threads(nt)
+    {
+        float* lut = (float*)malloc(sizeof(float) * (size_t)m * KSUB);
+        float* hd = (float*)malloc(sizeof(float) * (size_t)(k > 0 ? k : 1));
+        int32_t* hi = (int32_t*)malloc(sizeof(int32_t) * (size_t)(k > 0 ? k : 1));
+        float* pd = (float*)malloc(sizeof(float) * (size_t)(nprobe > 0 ? nprobe : 1));
+        int32_t* pi = (int32_t*)malloc(sizeof(int32_t) * (size_t)(nprobe > 0 ? nprobe : 1));
+        float* pod = (float*)malloc(sizeof(float) * (size_t)(nprobe > 0 ? nprobe : 1));
+        int32_t* poi = (int32_t*)malloc(sizeof(int32_t) * (size_t)(nprobe > 0 ? nprobe : 1));
+        unsigned char* probed = (unsigned char*)malloc((size_t)(nlist > 0 ? nlist : 1));
+#pragma omp for schedule(dynamic)
+        for (int64_t q = 0; q < nq; ++q) {
+            const float* qv = queries + q * d;
+            topk_t pt;
+            topk_init(&pt, nprobe, pd, pi);
+            for (int l = 0; l < nlist; ++l) topk_push(&pt, l2sq(qv, coarse + (int64_t)l * d, (int)d), l);
+            topk_write(&pt, pod, poi);
+            memset(probed, 0, (size_t)nlist);
+            for (int j = 0; j < nprobe; ++j) {
+                if (poi[j] >= 0) probed[poi[j]] = 1;
+                if (probes_out) probes_out[q * nprobe + j] = poi[j];
+            }
+            vko_compute_lut(centroids, m, dsub, qv, 1, lut);
+            topk_t t;
+            topk_init(&t, k, hd, hi);
+            for (int64_t i = 0; i < n; ++i)
+                if (probed[list_of[i]]) topk_push(&t, adc_one(lut, codes + i * m, m), (int32_t)i);
+            topk_write(&t, out_d + q * k, out_i + q * k);
+        }
+        free(lut);
+        free(hd);
+        free(hi);
+        free(pd);
+        free(pi);
+        free(pod);
+        free(poi);
+        free(probed);
+    }
+}
+
 void vko_topk_push_all(const float* dists, const int32_t* ids, int64_t count, int k, float* out_d,
                        int32_t* out_i) {
     float* hd = (float*)malloc(sizeof(float) * (size_t)(k > 0 ? k : 1));

@@ -57,6 +57,19 @@ double vko_recall_at_k(const int32_t* found, int64_t found_stride, const int32_t
 
 /* Streaming search over codes that arrive in blocks (large configs: the codes never exist on the host at
  * once). Per query one bounded top-k; feed() must be called with ascending, non-overlapping id ranges. */
+/* Half-precision LUT search (the library's VK_LUT_F16 definition; see vk_oracle.c): the scaled, half-rounded
+ * tables (as floats) with their per-query exponents, and the search over them. */
+void vko_compute_lut_h16(const float* centroids, int m, int dsub, const float* queries, int64_t nq, float* lut,
+                         int* exps);
+void vko_adc_search_h16(const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
+                        const float* queries, int64_t nq, int k, float* out_d, int32_t* out_i, int threads);
+
+/* IVF search (the library's IVF definition; see vk_oracle.c): the flat search restricted to the rows of each
+ * query's nprobe nearest lists. */
+void vko_ivf_search(const float* centroids, int m, int dsub, const uint8_t* codes, const int32_t* list_of, int64_t n,
+                    const float* coarse, int nlist, const float* queries, int64_t nq, int nprobe, int k,
+                    float* out_d, int32_t* out_i, int32_t* probes_out, int threads);
+
 typedef struct vko_stream vko_stream;
 vko_stream* vko_stream_create(const float* lut, int64_t nq, int m, int k);
 void vko_stream_feed(vko_stream* s, const uint8_t* codes, int64_t count, int64_t id_base, int threads);

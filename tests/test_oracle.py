@@ -155,3 +155,31 @@ def test_reference_arm_inputs_match_the_package():
         assert np.array_equal(bits(pq.centroids), bits(w.centroids)), name
         assert np.array_equal(codes, w.codes), name
         assert np.array_equal(bits(q), bits(w.queries)), name
+
+
+def test_h16_definition_restated_in_numpy(port):
+    """The oracle's half-precision LUT search against an independent numpy statement of the same definition
+    (numpy float16 conversion rounds to nearest even; sums in float32 in sub-space order)."""
+    rng = np.random.default_rng(11)
+    m, dsub, n, nq, k = 16, 8, 3_000, 7, 10
+    cent = (rng.normal(size=(m, 256, dsub)) * 30).astype(np.float32)
+    codes = rng.integers(0, 256, size=(n, m)).astype(np.uint8)
+    q = (rng.normal(size=(nq, m * dsub)) * 30).astype(np.float32)
+    raw = port.compute_lut(cent, q)
+    tab, exps = port.compute_lut_h16(cent, q)
+    for j in range(nq):
+        mx = raw[j].max()
+        _, E = np.frexp(np.float32(mx))
+        assert exps[j] == int(np.clip(15 - E, -64, 64))
+        scaled = (raw[j].astype(np.float64) * 2.0 ** exps[j]).astype(np.float32)
+        assert scaled.max() >= 2 ** 14 and scaled.max() < 2 ** 15
+        ref = scaled.astype(np.float16).astype(np.float32)
+        assert np.array_equal(bits(tab[j]), bits(ref))
+    d, i = port.adc_search_h16(cent, codes, q, k)
+    for j in range(nq):
+        acc = np.zeros(n, np.float32)
+        for s in range(m):
+            acc = acc + tab[j, s, codes[:, s]]
+        dist = (acc.astype(np.float64) * 2.0 ** -int(exps[j])).astype(np.float32)
+        order = np.lexsort((np.arange(n), dist))[:k]
+        assert np.array_equal(i[j], order) and np.array_equal(bits(d[j]), bits(dist[order]))

@@ -35,7 +35,11 @@ class DeviceInfo(C.Structure):
 
 class Tuning(C.Structure):
     _fields_ = [("scan_threads", C.c_int), ("blocks_per_query", C.c_int), ("queries_per_block", C.c_int),
-                ("vectors_per_step", C.c_int), ("early_abandon", C.c_int)]
+                ("vectors_per_step", C.c_int), ("early_abandon", C.c_int), ("lut_precision", C.c_int)]
+
+
+VK_LUT_F32 = 0
+VK_LUT_F16 = 1
 
 
 class Timings(C.Structure):
@@ -89,7 +93,21 @@ ABI = {
     "vk_pq_train_device": (C.c_int, [C.c_int, _vp, _i64, C.c_int, C.c_int, _i64, _u64, _vp, _vp]),
     "vk_gen_codes_device": (C.c_int, [C.c_int, _u64, _vp, C.c_int, C.c_int, _i64, _i64, _vp, _vp]),
     "vk_search_noalloc": (C.c_int, [_vp, _vp, _i64, C.c_int, C.POINTER(Tuning), _vp, _vp]),
+    "vk_coop_create": (C.c_int, [C.c_int, _i64, C.POINTER(_vp)]),
+    "vk_coop_ipc_handle": (C.c_int, [_vp, _vp]),
+    "vk_coop_attach_ipc": (C.c_int, [_vp, C.c_int, _vp]),
+    "vk_coop_attach": (C.c_int, [_vp, C.c_int, _vp]),
+    "vk_coop_destroy": (C.c_int, [_vp]),
+    "vk_search_device_coop": (C.c_int, [_vp, _vp, C.c_uint32, _vp, _i64, C.c_int, C.POINTER(Tuning), _vp, _vp]),
+    "vk_ivf_create": (C.c_int, [C.c_int, _vp, C.c_int, C.c_int, _vp, _i64, _vp, C.c_int, _vp, C.POINTER(_vp)]),
+    "vk_ivf_destroy": (C.c_int, [_vp]),
+    "vk_ivf_info": (C.c_int, [_vp, C.POINTER(_i64), C.POINTER(C.c_int), C.POINTER(_i64)]),
+    "vk_ivf_search": (C.c_int, [_vp, _vp, _i64, C.c_int, C.c_int, C.POINTER(Tuning), _vp, C.POINTER(Timings)]),
+    "vk_ivf_search_device": (C.c_int, [_vp, _vp, _i64, C.c_int, C.c_int, C.POINTER(Tuning), _vp, _vp]),
+    "vk_ivf_sync": (C.c_int, [_vp, _vp]),
+    "vk_ivf_assign_device": (C.c_int, [C.c_int, _vp, _i64, C.c_int, _vp, C.c_int, _vp, _vp]),
 }
+COOP_HANDLE_BYTES = 80  # VK_COOP_HANDLE_BYTES
 NOALLOC_SCRATCH_BYTES = 32 << 20  # VK_NOALLOC_SCRATCH_BYTES
 
 HOST_ABI = {

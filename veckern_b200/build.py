@@ -63,7 +63,7 @@ def build(verbose: bool = False, jobs: int | None = None) -> None:
     gxx = _tool("g++")
     nvcc = _nvcc()
     headers = _headers()
-    cu_srcs = [CSRC / "vk_abi.cu"] + sorted(CSRC.glob("scan_q*.cu"))
+    cu_srcs = [CSRC / "vk_abi.cu"] + sorted(CSRC.glob("scan_*.cu"))
     jobs_list = []
     objs = []
     for src in cu_srcs:

@@ -27,7 +27,7 @@ void ok(int code, const char* what) {
 }
 
 vk_tuning_t to_c(const Tuning& t) {
-    return vk_tuning_t{t.scan_threads, t.blocks_per_query, t.queries_per_block, t.vectors_per_step, 1};
+    return vk_tuning_t{t.scan_threads, t.blocks_per_query, t.queries_per_block, t.vectors_per_step, 1, VK_LUT_F32};
 }
 
 }  // namespace

@@ -8,10 +8,12 @@
 //   LUT        per query group of Q queries, contiguous, already in the shared-memory layout of the scan:
 //              Q = 1: [s][c]; Q = 2: [s][c][2]; Q = 4: [s][c][4]; Q = 8: two [s][c][4] tables (queries 0-3, 4-7).
 //              One code byte then fetches all Q queries' entries with one LDS.32/64/128 (two LDS.128 for Q = 8).
+//              Half-precision LUTs (Q = 4 or 8): [s][c][Q] halves, one LDS.64 / LDS.128 per code byte.
 //   partials   [query][chunk][k] (dist, id) lists, merged by merge_kernel.
 #pragma once
 #include <cfloat>
 #include <cstdint>
+#include <cuda_fp16.h>
 
 #include "vk_device.cuh"
 #include "warp_topk.cuh"
@@ -19,22 +21,27 @@
 namespace vk {
 
 // ------------------------------------------------------------------------------------------------ LUT builder
-// grid (m, groups), block 256: thread c computes centroid c of sub-space s for the Q queries of group g.
+// Block (s, g) of 256 threads: thread c computes centroid c of sub-space s for the Q queries of group g.
 // Arithmetic of the reference's l2sq (include/veckern/common.hpp:27-34): diff = q - c, acc += diff * diff in
 // j order, each operation rounded on its own (__fsub_rn / __fmul_rn / __fadd_rn: no FMA contraction).
 // Padded query slots (index >= nq) get 0. `bound` (optional): the pruned scan's per-query bounds, reset to +inf.
+// `pairs` (IVF): the group's queries are pairs[g * Q + qq].x (-1: padding) instead of g * Q + qq.
 template <int Q>
-__global__ void __launch_bounds__(256) lut_kernel(const float* __restrict__ centroids,
-                                                  const float* __restrict__ queries, int64_t nq, int m, int dsub,
-                                                  float* __restrict__ lut, uint32_t* __restrict__ bound,
-                                                  int2* __restrict__ glist, int* __restrict__ glock, int k) {
+__device__ __forceinline__ void lut_entries(const float* __restrict__ centroids, const float* __restrict__ queries,
+                                            int64_t nq, int m, int dsub, uint32_t* __restrict__ bound,
+                                            int2* __restrict__ glist, int* __restrict__ glock, int k, float* acc,
+                                            const int2* __restrict__ pairs = nullptr) {
     extern __shared__ float qsub[];  // [Q][dsub]
     const int s = blockIdx.x, g = blockIdx.y, c = threadIdx.x;
     const int64_t d = (int64_t)m * dsub;
+    auto query_of = [&](int qq) -> int64_t {
+        const int64_t qi = pairs ? (int64_t)pairs[(int64_t)g * Q + qq].x : (int64_t)g * Q + qq;
+        return qi >= 0 && qi < nq ? qi : -1;
+    };
     for (int t = threadIdx.x; t < Q * dsub; t += blockDim.x) {
         const int qq = t / dsub, j = t - qq * dsub;
-        const int64_t qi = (int64_t)g * Q + qq;
-        qsub[t] = qi < nq ? queries[qi * d + (int64_t)s * dsub + j] : 0.f;
+        const int64_t qi = query_of(qq);
+        qsub[t] = qi >= 0 ? queries[qi * d + (int64_t)s * dsub + j] : 0.f;
     }
     if (bound && s == 0) {  // reset the pruned scan's per-query state: bound +inf, empty global list, lock free
         for (int t = c; t < Q * k; t += blockDim.x) {
@@ -48,7 +55,6 @@ __global__ void __launch_bounds__(256) lut_kernel(const float* __restrict__ cent
     }
     __syncthreads();
     const float* cen = centroids + ((int64_t)s * KSUB + c) * dsub;
-    float acc[Q];
 #pragma unroll
     for (int qq = 0; qq < Q; ++qq) acc[qq] = 0.f;
     for (int j = 0; j < dsub; ++j) {
@@ -61,7 +67,18 @@ __global__ void __launch_bounds__(256) lut_kernel(const float* __restrict__ cent
     }
 #pragma unroll
     for (int qq = 0; qq < Q; ++qq)
-        if ((int64_t)g * Q + qq >= nq) acc[qq] = 0.f;
+        if (query_of(qq) < 0) acc[qq] = 0.f;
+}
+
+// grid (m, groups), block 256: the fp32 LUT of each query group in the scan layout.
+template <int Q>
+__global__ void __launch_bounds__(256) lut_kernel(const float* __restrict__ centroids,
+                                                  const float* __restrict__ queries, int64_t nq, int m, int dsub,
+                                                  float* __restrict__ lut, uint32_t* __restrict__ bound,
+                                                  int2* __restrict__ glist, int* __restrict__ glock, int k) {
+    const int s = blockIdx.x, g = blockIdx.y, c = threadIdx.x;
+    float acc[Q];
+    lut_entries<Q>(centroids, queries, nq, m, dsub, bound, glist, glock, k, acc);
     float* out = lut + (int64_t)g * Q * m * KSUB;
     const int e = s * KSUB + c;
     if constexpr (Q == 1) {
@@ -76,7 +93,103 @@ __global__ void __launch_bounds__(256) lut_kernel(const float* __restrict__ cent
     }
 }
 
+// grid (m, max items), block 256: the fp32 LUT of each IVF work item (the queries of its pair slots), in the scan
+// layout; blocks past the item count (known only on the device) return at once.
+template <int Q>
+__global__ void __launch_bounds__(256) ivf_lut_kernel(const float* __restrict__ centroids,
+                                                      const float* __restrict__ queries, int64_t nq, int m, int dsub,
+                                                      const int2* __restrict__ pairs, const int* __restrict__ nitems,
+                                                      float* __restrict__ lut) {
+    const int s = blockIdx.x, g = blockIdx.y, c = threadIdx.x;
+    if (g >= __ldg(nitems)) return;  // block-uniform
+    float acc[Q];
+    lut_entries<Q>(centroids, queries, nq, m, dsub, nullptr, nullptr, nullptr, 0, acc, pairs);
+    float* out = lut + (int64_t)g * Q * m * KSUB;
+    const int e = s * KSUB + c;
+    if constexpr (Q == 4) {
+        reinterpret_cast<float4*>(out)[e] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    } else {
+        static_assert(Q == 8, "IVF items hold 4 or 8 queries");
+        reinterpret_cast<float4*>(out)[e] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        reinterpret_cast<float4*>(out)[m * KSUB + e] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+}
+
+// ---- half-precision LUTs (lut_precision = VK_LUT_F16)
+// Per query: T[s][c] = the fp32 entry above; M = max over (s, c) of T; e = the power of two that puts M in
+// [2^14, 2^15) (lut_h16_exponent); entry = T * 2^e rounded to half (round to nearest even). The scan sums the
+// halves in fp32 in sub-space order exactly as the fp32 path sums fp32 entries, and reports sum * 2^-e: both
+// scalings are exact, so ordering by the scaled sums is ordering by the reported distances.
+// Exponent of the per-query scale from the bits of the query's largest entry (entries are >= +0).
+__host__ __device__ inline int lut_h16_exponent(uint32_t max_bits) {
+    const int ef = (int)((max_bits >> 23) & 0xffu);
+    if (max_bits == 0u || ef == 255) return 0;  // all entries zero (or not finite: outside the input contract)
+    if (ef == 0) return 64;                     // subnormal maximum: the largest scale
+    const int e = 15 - (ef - 126);              // M = f * 2^(ef - 126), f in [0.5, 1)
+    return e < -64 ? -64 : e > 64 ? 64 : e;
+}
+// 2^e as a float, for |e| <= 64 (exact).
+__device__ __forceinline__ float exp2_int(int e) { return __int_as_float((int)((uint32_t)(127 + e) << 23)); }
+
+// Pass 0: each query's largest entry, as float bits (atomicMax on the bits orders non-negative floats); qmax
+// zeroed before the launch.
+template <int Q>
+__global__ void __launch_bounds__(256) lut_max_kernel(const float* __restrict__ centroids,
+                                                      const float* __restrict__ queries, int64_t nq, int m, int dsub,
+                                                      uint32_t* __restrict__ qmax) {
+    __shared__ uint32_t red[Q];
+    const int g = blockIdx.y;
+    if (threadIdx.x < Q) red[threadIdx.x] = 0u;
+    float acc[Q];
+    lut_entries<Q>(centroids, queries, nq, m, dsub, nullptr, nullptr, nullptr, 0, acc);
+#pragma unroll
+    for (int qq = 0; qq < Q; ++qq) {
+        const uint32_t w = __reduce_max_sync(FULL, __float_as_uint(acc[qq]));
+        if ((threadIdx.x & (WARP - 1)) == 0) atomicMax(red + qq, w);
+    }
+    __syncthreads();
+    if (threadIdx.x < Q && (int64_t)g * Q + threadIdx.x < nq) atomicMax(qmax + (int64_t)g * Q + threadIdx.x, red[threadIdx.x]);
+}
+
+// Pass 1: the scaled half entries in the scan layout [s][c][Q] (Q = 4 or 8); blocks of sub-space 0 also store
+// each query's exponent and reset the pruned scan's state.
+template <int Q>
+__global__ void __launch_bounds__(256) lut_h16_kernel(const float* __restrict__ centroids,
+                                                      const float* __restrict__ queries, int64_t nq, int m, int dsub,
+                                                      const uint32_t* __restrict__ qmax, int* __restrict__ qexp,
+                                                      __half* __restrict__ lut, uint32_t* __restrict__ bound,
+                                                      int2* __restrict__ glist, int* __restrict__ glock, int k) {
+    static_assert(Q == 4 || Q == 8, "half LUTs are built for 4 or 8 queries per group");
+    const int s = blockIdx.x, g = blockIdx.y, c = threadIdx.x;
+    float acc[Q];
+    lut_entries<Q>(centroids, queries, nq, m, dsub, bound, glist, glock, k, acc);
+    __half h[Q];
+#pragma unroll
+    for (int qq = 0; qq < Q; ++qq) {
+        const int64_t qi = (int64_t)g * Q + qq;
+        const int e = qi < nq ? lut_h16_exponent(qmax[qi]) : 0;
+        if (s == 0 && c == 0 && qi < nq) qexp[qi] = e;
+        h[qq] = __float2half_rn(__fmul_rn(acc[qq], exp2_int(e)));
+    }
+    __half* out = lut + ((int64_t)g * m * KSUB + (int64_t)s * KSUB + c) * Q;
+    if constexpr (Q == 4) {
+        uint2 v;
+        v.x = (uint32_t)__half_as_ushort(h[0]) | ((uint32_t)__half_as_ushort(h[1]) << 16);
+        v.y = (uint32_t)__half_as_ushort(h[2]) | ((uint32_t)__half_as_ushort(h[3]) << 16);
+        *reinterpret_cast<uint2*>(out) = v;
+    } else {
+        uint4 v;
+        v.x = (uint32_t)__half_as_ushort(h[0]) | ((uint32_t)__half_as_ushort(h[1]) << 16);
+        v.y = (uint32_t)__half_as_ushort(h[2]) | ((uint32_t)__half_as_ushort(h[3]) << 16);
+        v.z = (uint32_t)__half_as_ushort(h[4]) | ((uint32_t)__half_as_ushort(h[5]) << 16);
+        v.w = (uint32_t)__half_as_ushort(h[6]) | ((uint32_t)__half_as_ushort(h[7]) << 16);
+        *reinterpret_cast<uint4*>(out) = v;
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ fused scan
+constexpr int COOP_MAX_PEERS = 15;  // shards of one cooperative search, besides this one
+
 struct ScanArgs {
     const uint4* codes;  // interleaved layout, n_pad rows
     const uint8_t* perm; // [n_pad] lane placement: position p holds row (p & ~63) + perm[p]
@@ -95,7 +208,34 @@ struct ScanArgs {
     int m, W, nq, groups, chunks, k, stages;
     int merge_slots;        // 1 or Q (see scan_smem_plan)
     long long wait_budget;  // SM cycles a bounded wait may take
+    // Cooperative sharded search (pruned scan): xb = this shard's exchange array, xpeer = the other shards'
+    // (peer or IPC-mapped device memory); entries (epoch << 32) | ~bound_bits, so atomicMax keeps the newest
+    // search's smallest bound; a stale epoch reads as +inf. npeers = 0 and xb = nullptr: no exchange.
+    unsigned long long* xb;
+    unsigned long long* xpeer[COOP_MAX_PEERS];
+    int npeers;
+    uint32_t epoch;
+    // IVF search (scan_kernel with IVF = true): work items come from an item table instead of (chunk, group).
+    const int* ivf_item_list;      // [items] the list an item scans
+    const int2* ivf_item_pairs;    // [items][Q] (query, probe slot) of the item's queries; (-1, -1) pads
+    const int64_t* ivf_list_off;   // [nlist] first position of each list (a multiple of 64)
+    const int* ivf_list_rows;      // [nlist] positions of each list (a multiple of 64)
+    const int32_t* ivf_ids;        // [n_pad] id of the row in each position's slot, -1 for padding
+    const int* ivf_nitems;         // number of items (written by the planning kernels)
+    int nprobe;
 };
+
+// Bound of query qi from the other shards of a cooperative search (+inf bits when there is none yet).
+__device__ __forceinline__ uint32_t coop_bound(const ScanArgs& a, int64_t qi) {
+    if (!a.xb) return 0x7f800000u;
+    const unsigned long long v = __ldcg(a.xb + qi);
+    return (uint32_t)(v >> 32) == a.epoch ? 0xffffffffu - (uint32_t)v : 0x7f800000u;
+}
+// Offers a lowered bound of query qi to the other shards (posted system-scope atomics over NVLink).
+__device__ __forceinline__ void coop_publish(const ScanArgs& a, int64_t qi, uint32_t bits) {
+    const unsigned long long v = ((unsigned long long)a.epoch << 32) | (unsigned long long)(0xffffffffu - bits);
+    for (int p = 0; p < a.npeers; ++p) atomicMax_system(a.xpeer[p] + qi, v);
+}
 
 // Shared-memory plan of scan_kernel; host and device compute it with the same function. merge_slots: how many
 // queries' warp lists the item-end merge stages at once (1 or Q).
@@ -109,18 +249,20 @@ struct ScanSmem {
 // fewer than 32 entries queued between tiles). Other m keep a per-tile queue of row indices into the stage buffer.
 constexpr int CARRY_CAP = 96;
 constexpr int CARRY_QWIDE = CARRY_CAP - 32;
+constexpr int CARRY_DEPTH0 = 8;  // queued pairs resume at sub-space 8 + 2 * (their 2-bit depth field)
 __host__ __device__ constexpr bool carry_queue(int m) { return m == 16; }
 // Rows of a pruned chunk, relative to its first 64-row window: 24 bits of a queue entry (with the query, 3 bits,
 // and the phase-A depth, 2 bits).
 constexpr int64_t CARRY_MAX_CHUNK_ROWS = int64_t(1) << 23;
 
 __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp, int nw, int stages, int k,
-                                                   bool prune, int merge_slots) {
+                                                   bool prune, int merge_slots, bool h16, bool ivf = false) {
     auto up = [](uint32_t x, uint32_t a) { return (x + a - 1) / a * a; };
     ScanSmem p;
-    p.lut_bytes = (uint32_t)Q * m * KSUB * 4u;
+    p.lut_bytes = (uint32_t)Q * m * KSUB * (h16 ? 2u : 4u);
     p.tile_bytes = (uint32_t)ilp * W * 512u;
-    p.stage_bytes = p.tile_bytes + (uint32_t)ilp * 32u;  // codes, then the tile's placement bytes
+    // codes, then the tile's placement bytes, then (IVF) the ids of the tile's 64-row window
+    p.stage_bytes = p.tile_bytes + (uint32_t)ilp * 32u + (ivf ? 256u : 0u);
     p.lut = 0;
     p.stage = up(p.lut_bytes, 128);
     p.scratch = up(p.stage + (uint32_t)nw * stages * p.stage_bytes, 128);
@@ -132,7 +274,7 @@ __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp,
     p.ring = up(p.queue + queue_bytes, 16);
     p.bars = up(p.ring + (uint32_t)nw * stages * 4u, 16);
     p.flags = p.bars + (uint32_t)(nw * stages + 1) * 8u;
-    p.total = up(p.flags + 16, 128);
+    p.total = up(p.flags + 16 + 64, 128);  // s_item, s_abort, s_tile; the item's (query, probe slot) pairs
     return p;
 }
 
@@ -152,12 +294,38 @@ __host__ __device__ constexpr int prune_first(int m) { return m <= 16 ? 8 : m <=
 __host__ __device__ constexpr int prune_last(int m) { return m <= 16 ? 12 : m <= 32 ? 16 : 28; }
 constexpr int PRUNE_DEEPEN = 8;
 
+// Adds the 2 halves of a 32-bit word to acc[0], acc[1]: the mixed-precision add of sm_100 (add.rn.f32.f16)
+// converts the half exactly to fp32 and rounds the sum once, so each is __fadd_rn(acc, __half2float(h)) in one
+// instruction instead of a conversion and an add.
+__device__ __forceinline__ float add_f32_f16(float acc, unsigned short h) {
+    float r;
+    asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(r) : "h"(h), "f"(acc));
+    return r;
+}
+__device__ __forceinline__ void add_half2(uint32_t w, float* acc) {
+    acc[0] = add_f32_f16(acc[0], (unsigned short)(w & 0xffffu));
+    acc[1] = add_f32_f16(acc[1], (unsigned short)(w >> 16));
+}
+
 // One sub-space lookup for Q queries: acc[q] += LUT_q[s][c], rounded per add, in s order.
-template <int Q>
+template <int Q, bool H16>
 __device__ __forceinline__ void lookup_add(const unsigned char* lut_smem, int mtab, int s, uint32_t c,
                                            float* acc) {
     const uint32_t e = (uint32_t)s * KSUB + c;
-    if constexpr (Q == 1) {
+    if constexpr (H16) {
+        static_assert(Q == 4 || Q == 8, "half LUTs hold 4 or 8 queries per entry");
+        if constexpr (Q == 4) {
+            const uint2 v = reinterpret_cast<const uint2*>(lut_smem)[e];
+            add_half2(v.x, acc);
+            add_half2(v.y, acc + 2);
+        } else {
+            const uint4 v = reinterpret_cast<const uint4*>(lut_smem)[e];
+            add_half2(v.x, acc);
+            add_half2(v.y, acc + 2);
+            add_half2(v.z, acc + 4);
+            add_half2(v.w, acc + 6);
+        }
+    } else if constexpr (Q == 1) {
         acc[0] = __fadd_rn(acc[0], reinterpret_cast<const float*>(lut_smem)[e]);
     } else if constexpr (Q == 2) {
         const float2 v = reinterpret_cast<const float2*>(lut_smem)[e];
@@ -184,13 +352,20 @@ __device__ __forceinline__ void lookup_add(const unsigned char* lut_smem, int mt
 }
 
 // Byte offset of query q's entry (s = 0, c = 0) in the group's LUT, and the stride between c entries.
-template <int Q>
+template <int Q, bool H16>
 __device__ __forceinline__ uint32_t lut_query_base(int q, int mtab) {
-    if constexpr (Q >= 4) return (uint32_t)(q >> 2) * (uint32_t)mtab * KSUB * 16u + (uint32_t)(q & 3) * 4u;
+    if constexpr (H16) return (uint32_t)q * 2u;
+    else if constexpr (Q >= 4) return (uint32_t)(q >> 2) * (uint32_t)mtab * KSUB * 16u + (uint32_t)(q & 3) * 4u;
     else return (uint32_t)q * 4u;
 }
-template <int Q>
-__host__ __device__ constexpr uint32_t lut_entry_bytes() { return Q >= 4 ? 16u : (uint32_t)Q * 4u; }
+template <int Q, bool H16>
+__host__ __device__ constexpr uint32_t lut_entry_bytes() { return H16 ? (uint32_t)Q * 2u : Q >= 4 ? 16u : (uint32_t)Q * 4u; }
+// One query's entry at byte address p of the shared LUT, as fp32.
+template <bool H16>
+__device__ __forceinline__ float lut_value(const unsigned char* p) {
+    if constexpr (H16) return __half2float(*reinterpret_cast<const __half*>(p));
+    else return *reinterpret_cast<const float*>(p);
+}
 
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int b) {
     return b < 4 ? v.x : b < 8 ? v.y : b < 12 ? v.z : v.w;
@@ -214,14 +389,22 @@ __device__ __forceinline__ uint32_t code_byte(const uint4& v, int b) { return (w
 //   and finished 32 at a time, each lane dropping out as soon as its sum exceeds T_q; otherwise the whole tile
 //   is finished with the Q-wide lookups. Results are unchanged.
 // MT: m when it is 16, 32 or 64 (fully unrolled sub-space loop), 0 for any other m.
-// Block shape: two blocks of 8 warps share an SM when the group's LUT is at most 80 KB; a larger LUT leaves room
+// Block shape: two blocks of 8 warps share an SM when the group's fp32 LUT is at most 80 KB; a larger LUT leaves room
 // for one block, which then has 16 warps. Either way 16 warps per SM, registers capped at 128.
-__host__ __device__ constexpr int scan_warps(int Q, int MT) { return Q * (MT ? MT : 16) * KSUB * 4 <= 80 * 1024 ? 8 : 16; }
-template <int Q, int MT>
-constexpr int scan_min_blocks() { return scan_warps(Q, MT) == 8 ? 2 : 1; }
+// Half-precision LUTs always take 16-warp blocks: two 8-warp blocks with their own 64 KB LUTs, rings and queues do
+// not fit one SM's shared memory together, which left one 8-warp block per SM (measured: 12.5 % warps active).
+__host__ __device__ constexpr int scan_warps(int Q, int MT, bool H16 = false) {
+    return !H16 && Q * (MT ? MT : 16) * KSUB * 4 <= 80 * 1024 ? 8 : 16;
+}
+template <int Q, int MT, bool H16>
+constexpr int scan_min_blocks() { return scan_warps(Q, MT, H16) == 8 ? 2 : 1; }
 
-template <int Q, int MT, int ILP, int S, int NW, bool PRUNE>
-__global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel(const ScanArgs a) {
+// H16: half-precision LUT entries (Q = 4 or 8, m = 16, 32 or 64), summed in fp32 like the fp32 entries.
+// IVF: items are (list, up to Q queries probing it) from the IVF item table; ids come from the index's id array.
+template <int Q, int MT, int ILP, int S, int NW, bool PRUNE, bool H16 = false, bool IVF = false>
+__global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_kernel(const ScanArgs a) {
+    static_assert(!IVF || (ILP <= 2 && !H16), "IVF items start on 64-row windows; fp32 LUTs");
+    static_assert(!H16 || (MT != 0 && (Q == 4 || Q == 8)), "half LUTs: m = 16, 32, 64 and 4 or 8 queries");
     static_assert(!PRUNE || MT != 0, "the pruned scan is specialised for m = 16, 32, 64");
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int W_T = MT ? (MT + 15) / 16 : 0;
@@ -230,13 +413,14 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                   "phase A stops at even sub-spaces: phase B fetches sub-spaces in pairs inside one 16-byte word");
     const int m = MT ? MT : a.m;
     const int W = MT ? W_T : a.W;
-    const ScanSmem plan = scan_smem_plan(Q, m, W, ILP, NW, a.stages, a.k, PRUNE, a.merge_slots);
+    const ScanSmem plan = scan_smem_plan(Q, m, W, ILP, NW, a.stages, a.k, PRUNE, a.merge_slots, H16, IVF);
     unsigned char* lut_smem = smem + plan.lut;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + plan.bars);
     uint64_t* lut_bar = bars + NW * a.stages;
     int* s_item = reinterpret_cast<int*>(smem + plan.flags);
     int* s_abort = s_item + 1;
     int* s_tile = s_item + 2;
+    int2* s_pairs = reinterpret_cast<int2*>(smem + plan.flags + 16);  // IVF: the item's (query, probe slot) pairs
     int2* scratch = reinterpret_cast<int2*>(smem + plan.scratch);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -252,7 +436,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
     }
     __syncthreads();
 
-    const int items = a.groups * a.chunks;
+    const int items = IVF ? __ldg(a.ivf_nitems) : a.groups * a.chunks;
     const int64_t tile_rows = 32 * ILP;
     uint32_t issued = 0, consumed = 0, lut_phase = 0;  // issued: lane 0 only
     uint32_t lut_pending = ~0u;  // thread 0: parity of a LUT copy not yet seen complete (~0u: none)
@@ -263,12 +447,25 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
             *s_item = atomicAdd(a.work_counter, 1);
             *s_tile = 0;
         }
+        if constexpr (IVF) {
+            __syncthreads();  // s_item is visible
+            const int it = *s_item;
+            if (threadIdx.x < Q) s_pairs[threadIdx.x] = it < items ? a.ivf_item_pairs[(int64_t)it * Q + threadIdx.x]
+                                                                   : make_int2(-1, -1);
+        }
         __syncthreads();  // (A) previous item finished by every warp; the LUT may be replaced
         const int item = *s_item;
         if (item >= items || *s_abort) break;
-        const int chunk = item / a.groups, g = item - chunk * a.groups;
+        // flat: (chunk, query group); IVF: the item's list, and its own LUT (g = item)
+        const int chunk = IVF ? 0 : item / a.groups, g = IVF ? item : item - chunk * a.groups;
+        const int list = IVF ? a.ivf_item_list[item] : 0;
+        // global index of the item's query q (-1: padding); IVF: the probe slot its list is for that query
+        auto qidx = [&](int q) -> int64_t {
+            if constexpr (IVF) return s_pairs[q].x;
+            else return (int64_t)g * Q + q < a.nq ? (int64_t)g * Q + q : -1;
+        };
 
-        if (g != cur_g) {
+        if (IVF || g != cur_g) {
             if (threadIdx.x == 0) {
                 fence_proxy_async_smem();
                 const unsigned char* src =
@@ -297,13 +494,15 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
         for (int q = 0; q < Q; ++q) {
             top[q].init();
             if constexpr (PRUNE) {
-                const int64_t qi = (int64_t)g * Q + q;
-                known[q] = qi < a.nq ? __uint_as_float(__ldcg(a.bound + qi)) : -1.f;
+                const int64_t qi = qidx(q);
+                known[q] = qi >= 0 ? __uint_as_float(min(__ldcg(a.bound + qi), coop_bound(a, qi))) : -1.f;
             }
         }
 
-        const int64_t row_begin = chunk == 0 ? 0 : a.first_len + (int64_t)(chunk - 1) * a.chunk_len;
-        const int64_t row_end = min(a.first_len + (int64_t)chunk * a.chunk_len, a.n_pad);
+        const int64_t row_begin = IVF ? a.ivf_list_off[list]
+                                      : chunk == 0 ? 0 : a.first_len + (int64_t)(chunk - 1) * a.chunk_len;
+        const int64_t row_end = IVF ? row_begin + a.ivf_list_rows[list]
+                                    : min(a.first_len + (int64_t)chunk * a.chunk_len, a.n_pad);
         const int64_t t_begin = row_begin / tile_rows;
         const int ntiles = (int)(row_end / tile_rows - t_begin);
 
@@ -322,14 +521,14 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
             float x = __int_as_float(ent.x);
             const uint32_t meta = (uint32_t)ent.y;
             const int q = (int)((meta >> 24) & 7u);
-            int s = SA + 2 * (int)(meta >> 27);
+            int s = CARRY_DEPTH0 + 2 * (int)(meta >> 27);
             uint32_t lo = (uint32_t)ent.z, hi = (uint32_t)ent.w;
             // the query's bound now: min(the warp's view of its global bound, the warp list's k-th distance)
             float bq = fminf(known[0], top[0].thr_d);
 #pragma unroll
             for (int qq = 1; qq < Q; ++qq)
                 if (q == qq) bq = fminf(known[qq], top[qq].thr_d);
-            const unsigned char* lq = lut_smem + lut_query_base<Q>(q, MT);
+            const unsigned char* lq = lut_smem + lut_query_base<Q, H16>(q, MT);
             bool live = in && !(x > bq);  // the bound may have dropped since the pair was queued
 #pragma unroll
             for (int t = 0; t < (MT - SA) / 2; ++t) {
@@ -339,9 +538,8 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                     const uint32_t c0 = lo & 0xffu, c1 = (lo >> 8) & 0xffu;
                     lo = __funnelshift_r(lo, hi, 16);
                     hi >>= 16;
-                    const float v0 = *reinterpret_cast<const float*>(lq + ((uint32_t)s * KSUB + c0) * lut_entry_bytes<Q>());
-                    const float v1 =
-                        *reinterpret_cast<const float*>(lq + ((uint32_t)(s + 1) * KSUB + c1) * lut_entry_bytes<Q>());
+                    const float v0 = lut_value<H16>(lq + ((uint32_t)s * KSUB + c0) * lut_entry_bytes<Q, H16>());
+                    const float v1 = lut_value<H16>(lq + ((uint32_t)(s + 1) * KSUB + c1) * lut_entry_bytes<Q, H16>());
                     x = __fadd_rn(x, v0);
                     live = !(x > bq);
                     x = __fadd_rn(x, v1);
@@ -350,7 +548,10 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                 }
             }
             if (__any_sync(FULL, live)) {  // usually every pair of the batch was abandoned
-                const int32_t id = carry_id0 + (int32_t)(meta & 0xffffffu);
+                const int32_t id = IVF ? (in ? __ldg(a.ivf_ids + (row_begin & ~(int64_t)(PLACE_WINDOW - 1)) +
+                                                     (int64_t)(meta & 0xffffffu))
+                                             : -1)
+                                       : carry_id0 + (int32_t)(meta & 0xffffffu);
 #pragma unroll
                 for (int qq = 0; qq < Q; ++qq) {
                     if (__any_sync(FULL, live && q == qq)) top[qq].offer(x, id, live && q == qq, a.k);
@@ -377,6 +578,10 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                 mbar_arrive_expect_tx(my_bars + slot, plan.stage_bytes);
                 bulk_g2s(dst, a.codes + (t_begin + t) * tile_rows * W, plan.tile_bytes, my_bars + slot);
                 bulk_g2s(dst + plan.tile_bytes, a.perm + (t_begin + t) * tile_rows, (uint32_t)tile_rows, my_bars + slot);
+                if constexpr (IVF)  // the ids of the tile's 64-row window (1 KB-aligned source: 16-byte rule holds)
+                    bulk_g2s(dst + plan.tile_bytes + (uint32_t)tile_rows,
+                             a.ivf_ids + (((t_begin + t) * tile_rows) & ~(int64_t)(PLACE_WINDOW - 1)), 256u,
+                             my_bars + slot);
                 ++issued;
             } else {
                 my_ring[slot] = -1;
@@ -407,7 +612,16 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
             const int64_t tile_row0 = (t_begin + tile) * tile_rows;
             // global id of the row at tile position r (lane placement within 64-row windows)
             auto row_id = [&](int r) {
-                return (int32_t)(a.id_base + ((tile_row0 + r) & ~(int64_t)(PLACE_WINDOW - 1)) + st_perm[r]);
+                if constexpr (IVF) {  // the slot's id from the window's ids staged with the tile (-1: padding)
+                    return reinterpret_cast<const int32_t*>(st_perm + tile_rows)[st_perm[r]];
+                } else {
+                    return (int32_t)(a.id_base + ((tile_row0 + r) & ~(int64_t)(PLACE_WINDOW - 1)) + st_perm[r]);
+                }
+            };
+            // rows past n (flat) or padding slots of a list (IVF) are computed but never offered
+            auto row_valid = [&](int r) {
+                if constexpr (IVF) return row_id(r) >= 0;
+                else return tile_row0 + r < a.n;
             };
 
             if constexpr (!PRUNE) {
@@ -430,21 +644,24 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                             const int s = ww * 16 + b;
                             if (!MT && s >= m) break;
 #pragma unroll
-                            for (int u = 0; u < ILP; ++u) lookup_add<Q>(lut_smem, m, s, code_byte(cv[u], b), acc[u]);
+                            for (int u = 0; u < ILP; ++u) lookup_add<Q, H16>(lut_smem, m, s, code_byte(cv[u], b), acc[u]);
                         }
                     }
                 }
                 int32_t ids[ILP];
 #pragma unroll
-                for (int u = 0; u < ILP; ++u) ids[u] = row_id(u * 32 + lane);
-                __syncwarp();  // every lane has consumed the slot (codes and placement bytes)
+                bool valid[ILP];
+#pragma unroll
+                for (int u = 0; u < ILP; ++u) {  // both read the stage slot (IVF), so before it is refilled
+                    ids[u] = row_id(u * 32 + lane);
+                    valid[u] = row_valid(u * 32 + lane);
+                }
+                __syncwarp();  // every lane has consumed the slot (codes, placement bytes, ids)
                 if (lane == 0) refill();
 
                 bool any = false;
-                bool valid[ILP];
 #pragma unroll
                 for (int u = 0; u < ILP; ++u) {
-                    valid[u] = tile_row0 + u * 32 + lane < a.n;
 #pragma unroll
                     for (int q = 0; q < Q; ++q) any |= valid[u] && top[q].admits(acc[u][q], ids[u]);
                 }
@@ -458,7 +675,10 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                 // The query group's global bounds, loaded now (lane q: query q) so that the L2 latency hides
                 // behind phase A; other warps and blocks keep lowering them.
                 float gb = __int_as_float(0x7f800000);
-                if (lane < Q && (int64_t)g * Q + lane < a.nq) gb = __uint_as_float(__ldcg(a.bound + (int64_t)g * Q + lane));
+                if (lane < Q) {
+                    const int64_t qi = qidx(lane);
+                    if (qi >= 0) gb = __uint_as_float(min(__ldcg(a.bound + qi), coop_bound(a, qi)));
+                }
                 // ---- phase A: sub-spaces [0, SA) of every row, all Q queries per fetch
                 float acc[ILP][Q];
 #pragma unroll
@@ -473,7 +693,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                         for (int u = 0; u < ILP; ++u) cv[u] = st[(u * W_T + s / 16) * 32 + lane];
                     }
 #pragma unroll
-                    for (int u = 0; u < ILP; ++u) lookup_add<Q>(lut_smem, MT, s, code_byte(cv[u], s % 16), acc[u]);
+                    for (int u = 0; u < ILP; ++u) lookup_add<Q, H16>(lut_smem, MT, s, code_byte(cv[u], s % 16), acc[u]);
                 };
                 static_for<SA>(phase_a);
                 float bnd[Q];
@@ -485,7 +705,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                 // ---- surviving (row, query) pairs: this lane's pair (u, q) is alive while its partial sum is not
                 // above the query's bound (recomputed where needed rather than kept as ballots: registers)
                 auto alive = [&](int u, int q) {
-                    return tile_row0 + u * 32 + lane < a.n && !(acc[u][q] > bnd[q]);
+                    return row_valid(u * 32 + lane) && !(acc[u][q] > bnd[q]);
                 };
                 int total = 0;
                 auto vote = [&]() {
@@ -550,19 +770,29 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                                 }
                             }
                         __syncwarp();
-                        const uint32_t dsel = (uint32_t)(dep - SA) / 2u;
+                        // entries hold the codes of sub-spaces d0 .. 15 (8 bytes at most): a pair voted at a depth
+                        // below CARRY_DEPTH0 first gets its sub-spaces dep .. CARRY_DEPTH0 - 1 added here
+                        const int d0 = dep > CARRY_DEPTH0 ? dep : CARRY_DEPTH0;
+                        const uint32_t dsel = (uint32_t)(d0 - CARRY_DEPTH0) / 2u;
                         // the chunk's first window starts row_begin % 64 rows before it (windows are 64-aligned)
                         const uint32_t tile_rel = (uint32_t)(row_begin & (PLACE_WINDOW - 1)) + (uint32_t)tile * (uint32_t)tile_rows;
                         for (int e = first + lane; e < qcnt; e += 32) {
                             uint32_t* ent = reinterpret_cast<uint32_t*>(my_carry + e);
                             const uint32_t y = ent[1];
                             const uint32_t r = y & 0xffffu;
-                            const uint2 zw = reinterpret_cast<const uint2*>(st + r)[1];  // bytes 8..15 of row r
-                            const uint32_t lo = dep == 8 ? zw.x : dep == 10 ? __funnelshift_r(zw.x, zw.y, 16) : zw.y;
-                            const uint32_t hi = dep == 8 ? zw.y : dep == 10 ? zw.y >> 16 : 0u;
+                            const uint4 w = st[r];  // the row's 16 sub-codes
+                            float x = __uint_as_float(ent[0]);
+                            if (dep < CARRY_DEPTH0) {  // warp-uniform
+                                const unsigned char* lq = lut_smem + lut_query_base<Q, H16>((int)(y >> 24), MT);
+                                for (int sb = dep; sb < CARRY_DEPTH0; ++sb)
+                                    x = __fadd_rn(x, lut_value<H16>(lq + ((uint32_t)sb * KSUB + code_byte(w, sb)) *
+                                                                             lut_entry_bytes<Q, H16>()));
+                            }
+                            const uint32_t lo = d0 == 8 ? w.z : d0 == 10 ? __funnelshift_r(w.z, w.w, 16) : w.w;
+                            const uint32_t hi = d0 == 8 ? w.w : d0 == 10 ? w.w >> 16 : 0u;
                             const uint32_t rel = ((tile_rel + r) & ~(uint32_t)(PLACE_WINDOW - 1)) + st_perm[r];
                             reinterpret_cast<uint4*>(ent)[0] =
-                                make_uint4(ent[0], rel | (y & (7u << 24)) | (dsel << 27), lo, hi);
+                                make_uint4(__float_as_uint(x), rel | (y & (7u << 24)) | (dsel << 27), lo, hi);
                         }
                     }
                     __syncwarp();  // the stage slot is free: queued pairs carry their codes
@@ -606,7 +836,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
 #pragma unroll
                         for (int qq = 1; qq < Q; ++qq)
                             if (q == qq) bq = bnd[qq];
-                        const unsigned char* lq = lut_smem + lut_query_base<Q>(q, MT);
+                        const unsigned char* lq = lut_smem + lut_query_base<Q, H16>(q, MT);
                         const uint4* rowp = st + (r >> 5) * W_T * 32 + (r & 31);
                         uint4 cw = make_uint4(0, 0, 0, 0);
 #pragma unroll
@@ -619,8 +849,8 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                             }
                             if (live) {
                                 const uint32_t c0 = code_byte(cw, s % 16), c1 = code_byte(cw, (s + 1) % 16);
-                                const float v0 = *reinterpret_cast<const float*>(lq + ((uint32_t)s * KSUB + c0) * lut_entry_bytes<Q>());
-                                const float v1 = *reinterpret_cast<const float*>(lq + ((uint32_t)(s + 1) * KSUB + c1) * lut_entry_bytes<Q>());
+                                const float v0 = lut_value<H16>(lq + ((uint32_t)s * KSUB + c0) * lut_entry_bytes<Q, H16>());
+                                const float v1 = lut_value<H16>(lq + ((uint32_t)(s + 1) * KSUB + c1) * lut_entry_bytes<Q, H16>());
                                 x = __fadd_rn(x, v0);
                                 live = !(x > bq);
                                 x = __fadd_rn(x, v1);
@@ -651,8 +881,12 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                 // Publish improved list thresholds as global bounds for the other warps and blocks.
 #pragma unroll
                 for (int q = 0; q < Q; ++q) {
-                    if (top[q].thr_d < known[q]) {
-                        if (lane == 0) atomicMin(a.bound + (int64_t)g * Q + q, __float_as_uint(top[q].thr_d));
+                    if (top[q].thr_d < known[q]) {  // never for padded slots (known -1)
+                        if (lane == 0) {
+                            const int64_t qi = qidx(q);
+                            atomicMin(a.bound + qi, __float_as_uint(top[q].thr_d));
+                            coop_publish(a, qi, __float_as_uint(top[q].thr_d));
+                        }
                         known[q] = top[q].thr_d;
                     }
                 }
@@ -676,8 +910,8 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
         __syncthreads();  // (B) all warps finished the item's tiles; s_abort is stable
         if (*s_abort) continue;  // uniform: the next (A) exits the loop
         // Merge the NW warp lists of each query into the item's partial list: merge_slots queries at a time,
-        // query q0 + j merged by warp j.
-        auto merge_and_publish = [&](int64_t qi, const int2* slot_lists, float kb) {
+        // query q0 + j merged by warp j. qi: the query's global index, ql: its slot in the item.
+        auto merge_and_publish = [&](int64_t qi, int ql, const int2* slot_lists, float kb) {
             WarpTopK<S> mt;
             mt.init();
             // Pairs above kb (an upper bound of the query's final k-th distance) cannot be in the result, so they
@@ -688,7 +922,9 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                 const int2 e = j < total ? slot_lists[j] : make_int2(0x7f800000, SENTINEL_ID);
                 mt.offer(__int_as_float(e.x), e.y, j < total && !(__int_as_float(e.x) > kb), a.k);
             }
-            mt.store(a.part + (qi * a.chunks + chunk) * a.k, a.k);  // this item's own list
+            // this item's own list: [query][chunk][k] (flat), [query][probe slot][k] (IVF)
+            if constexpr (IVF) mt.store(a.part + (qi * a.nprobe + s_pairs[ql].y) * a.k, a.k);
+            else mt.store(a.part + (qi * a.chunks + chunk) * a.k, a.k);
             if constexpr (PRUNE) {
                 // Fold the item's list into the query's global list of the best pairs seen so far, whose k-th
                 // distance bounds the query for every other warp. Chunks cover disjoint rows, so the union has
@@ -713,30 +949,33 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
                     if (lane == 0) atomicExch(a.glock + qi, 0);
                 }
                 if (lane == 0 && mt.thr_i != SENTINEL_ID && mt.thr_d < kb)
+                {
                     atomicMin(a.bound + qi, __float_as_uint(mt.thr_d));
+                    coop_publish(a, qi, __float_as_uint(mt.thr_d));
+                }
             }
         };
         if (a.merge_slots >= Q) {
 #pragma unroll
             for (int q = 0; q < Q; ++q) top[q].store(scratch + (q * NW + warp) * a.k, a.k);
             __syncthreads();
-            const int64_t qi = (int64_t)g * Q + warp;
+            const int64_t qi = warp < Q ? qidx(warp) : -1;
             float kb = __int_as_float(0x7f800000);
             if constexpr (PRUNE) {
 #pragma unroll
                 for (int q = 0; q < Q; ++q)
                     if (warp == q) kb = known[q];
             }
-            if (warp < Q && qi < a.nq) merge_and_publish(qi, scratch + warp * NW * a.k, kb);
+            if (qi >= 0) merge_and_publish(qi, warp, scratch + warp * NW * a.k, kb);
             __syncthreads();
         } else {
 #pragma unroll
             for (int q = 0; q < Q; ++q) {
-                const int64_t qi = (int64_t)g * Q + q;
-                if (qi < a.nq) {  // uniform
+                const int64_t qi = qidx(q);
+                if (qi >= 0) {  // uniform
                     top[q].store(scratch + warp * a.k, a.k);
                     __syncthreads();
-                    if (warp == 0) merge_and_publish(qi, scratch, PRUNE ? known[q] : __int_as_float(0x7f800000));
+                    if (warp == 0) merge_and_publish(qi, q, scratch, PRUNE ? known[q] : __int_as_float(0x7f800000));
                     __syncthreads();
                 }
             }
@@ -752,10 +991,11 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT>()) scan_kernel
 // One warp per query: the k best of `lists` sorted lists of k_in entries (entry (q, l, j) at
 // in[q * qstride + l * lstride + j]); entries with id < 0 are padding. Output ascending, empty slots {+inf, -1}
 // (the reference's host fix-up, src/cuda/searcher.cu:514-517).
+// qexp (optional): per-query exponents of half-precision LUTs; distances are scaled by 2^-qexp[q] on output.
 template <int S>
 __global__ void __launch_bounds__(128) merge_kernel(const int2* __restrict__ in, int64_t nq, int lists, int k_in,
                                                     int64_t qstride, int64_t lstride, int k,
-                                                    int2* __restrict__ out) {
+                                                    int2* __restrict__ out, const int* __restrict__ qexp) {
     const int lane = threadIdx.x & 31;
     const int64_t q = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (q >= nq) return;  // warp-uniform
@@ -772,12 +1012,14 @@ __global__ void __launch_bounds__(128) merge_kernel(const int2* __restrict__ in,
         }
         top.offer(__int_as_float(e.x), e.y, j < total && e.y >= 0, k);
     }
+    const float scale = qexp ? exp2_int(-qexp[q]) : 1.f;
 #pragma unroll
     for (int r = 0; r < S; ++r) {
         const int e = r * 32 + lane;
         if (e < k) {
             const bool pad = top.id[r] == SENTINEL_ID;
-            out[q * k + e] = pad ? make_int2(0x7f800000, -1) : make_int2(__float_as_int(top.d[r]), top.id[r]);
+            out[q * k + e] = pad ? make_int2(0x7f800000, -1)
+                                 : make_int2(__float_as_int(qexp ? __fmul_rn(top.d[r], scale) : top.d[r]), top.id[r]);
         }
     }
 }
@@ -788,7 +1030,7 @@ __global__ void __launch_bounds__(128) merge_kernel(const int2* __restrict__ in,
 template <int S>
 __global__ void __launch_bounds__(256) merge_wide_kernel(const int2* __restrict__ in, int64_t nq, int lists, int k_in,
                                                          int64_t qstride, int64_t lstride, int k,
-                                                         int2* __restrict__ out) {
+                                                         int2* __restrict__ out, const int* __restrict__ qexp) {
     constexpr int NWM = 8;
     __shared__ int2 part[NWM * 32 * S];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -817,12 +1059,14 @@ __global__ void __launch_bounds__(256) merge_wide_kernel(const int2* __restrict_
         const int2 e = j < NWM * k ? part[j] : make_int2(0x7f800000, SENTINEL_ID);
         fin.offer(__int_as_float(e.x), e.y, j < NWM * k, k);
     }
+    const float scale = qexp ? exp2_int(-qexp[q]) : 1.f;
 #pragma unroll
     for (int r = 0; r < S; ++r) {
         const int e = r * 32 + lane;
         if (e < k) {
             const bool pad = fin.id[r] == SENTINEL_ID;
-            out[q * k + e] = pad ? make_int2(0x7f800000, -1) : make_int2(__float_as_int(fin.d[r]), fin.id[r]);
+            out[q * k + e] = pad ? make_int2(0x7f800000, -1)
+                                 : make_int2(__float_as_int(qexp ? __fmul_rn(fin.d[r], scale) : fin.d[r]), fin.id[r]);
         }
     }
 }

@@ -1,5 +1,5 @@
-// Instantiation table of scan_kernel<Q, MT, ILP, S, NW = scan_warps(Q, MT), PRUNE>. Each Q lives in its own translation unit
-// (scan_q{1,2,4,8}.cu) so nvcc compiles them in parallel.
+// Instantiation table of scan_kernel<Q, MT, ILP, S, NW = scan_warps(Q, MT, H16), PRUNE, H16>. Each Q lives in its own
+// translation unit (scan_q{1,2,4,8}.cu; half-precision LUTs: scan_h{4,8}.cu) so nvcc compiles them in parallel.
 #pragma once
 #include "kernels.cuh"
 
@@ -9,6 +9,12 @@ namespace vk {
 // none (the pruned scan exists for mt in {16, 32, 64} and ilp in {1, 2}).
 template <int Q>
 const void* scan_kernel_for(int mt, int ilp, int s, bool prune);
+// Half-precision LUTs: Q in {4, 8}, mt in {16, 32, 64}, ilp in {1, 2}.
+template <int Q>
+const void* scan_kernel_h16_for(int mt, int ilp, int s, bool prune);
+// IVF items: Q in {4, 8}, mt in {16, 32}, ilp in {1, 2}, fp32 LUTs.
+template <int Q>
+const void* scan_kernel_ivf_for(int mt, int ilp, int s, bool prune);
 
 #define VK_SCAN_CASE(Q, MT, ILP, S, P)            \
     case (P) * 10000 + MT * 100 + ILP * 10 + S: \
@@ -31,6 +37,43 @@ const void* scan_kernel_for(int mt, int ilp, int s, bool prune);
             VK_SCAN_CASES_MT_PRUNE(Q, 64)                               \
             default: return nullptr;                                    \
         }                                                               \
+    }
+
+#define VK_SCAN_CASE_H(Q, MT, ILP, S, P)          \
+    case (P) * 10000 + MT * 100 + ILP * 10 + S: \
+        return reinterpret_cast<const void*>(&scan_kernel<Q, MT, ILP, S, scan_warps(Q, MT, true), P, true>);
+#define VK_SCAN_CASES_H_S(Q, MT, ILP, P) VK_SCAN_CASE_H(Q, MT, ILP, 1, P) VK_SCAN_CASE_H(Q, MT, ILP, 2, P) VK_SCAN_CASE_H(Q, MT, ILP, 4, P)
+#define VK_SCAN_CASES_H_MT(Q, MT)                                                                          \
+    VK_SCAN_CASES_H_S(Q, MT, 1, false) VK_SCAN_CASES_H_S(Q, MT, 2, false) VK_SCAN_CASES_H_S(Q, MT, 1, true) \
+        VK_SCAN_CASES_H_S(Q, MT, 2, true)
+
+#define VK_SCAN_TABLE_H(Q)                                                  \
+    template <>                                                             \
+    const void* scan_kernel_h16_for<Q>(int mt, int ilp, int s, bool prune) { \
+        switch ((prune ? 10000 : 0) + mt * 100 + ilp * 10 + s) {            \
+            VK_SCAN_CASES_H_MT(Q, 16)                                       \
+            VK_SCAN_CASES_H_MT(Q, 32)                                       \
+            VK_SCAN_CASES_H_MT(Q, 64)                                       \
+            default: return nullptr;                                        \
+        }                                                                   \
+    }
+
+#define VK_SCAN_CASE_I(Q, MT, ILP, S, P)          \
+    case (P) * 10000 + MT * 100 + ILP * 10 + S: \
+        return reinterpret_cast<const void*>(&scan_kernel<Q, MT, ILP, S, scan_warps(Q, MT), P, false, true>);
+#define VK_SCAN_CASES_I_S(Q, MT, ILP, P) VK_SCAN_CASE_I(Q, MT, ILP, 1, P) VK_SCAN_CASE_I(Q, MT, ILP, 2, P) VK_SCAN_CASE_I(Q, MT, ILP, 4, P)
+#define VK_SCAN_CASES_I_MT(Q, MT)                                                                          \
+    VK_SCAN_CASES_I_S(Q, MT, 1, false) VK_SCAN_CASES_I_S(Q, MT, 2, false) VK_SCAN_CASES_I_S(Q, MT, 1, true) \
+        VK_SCAN_CASES_I_S(Q, MT, 2, true)
+
+#define VK_SCAN_TABLE_I(Q)                                                  \
+    template <>                                                             \
+    const void* scan_kernel_ivf_for<Q>(int mt, int ilp, int s, bool prune) { \
+        switch ((prune ? 10000 : 0) + mt * 100 + ilp * 10 + s) {            \
+            VK_SCAN_CASES_I_MT(Q, 16)                                       \
+            VK_SCAN_CASES_I_MT(Q, 32)                                       \
+            default: return nullptr;                                        \
+        }                                                                   \
     }
 
 }  // namespace vk

@@ -23,6 +23,7 @@
 
 #include "../../include/vk_abi.h"
 #include "aux_kernels.cuh"
+#include "ivf_kernels.cuh"
 #include "host/index_file.h"
 #include "kernels.cuh"
 #include "scan_dispatch.cuh"
@@ -112,7 +113,14 @@ const char* variant_name(int v) {
     return v >= 0 && v <= 8 ? names[v] : "unknown";
 }
 
-const void* scan_kernel_ptr(int Q, int mt, int ilp, int s, bool prune) {
+const void* scan_kernel_ptr(int Q, int mt, int ilp, int s, bool prune, bool h16) {
+    if (h16) {
+        switch (Q) {
+            case 4: return vk::scan_kernel_h16_for<4>(mt, ilp, s, prune);
+            case 8: return vk::scan_kernel_h16_for<8>(mt, ilp, s, prune);
+            default: return nullptr;
+        }
+    }
     switch (Q) {
         case 1: return vk::scan_kernel_for<1>(mt, ilp, s, prune);
         case 2: return vk::scan_kernel_for<2>(mt, ilp, s, prune);
@@ -120,6 +128,16 @@ const void* scan_kernel_ptr(int Q, int mt, int ilp, int s, bool prune) {
         case 8: return vk::scan_kernel_for<8>(mt, ilp, s, prune);
         default: return nullptr;
     }
+}
+
+const void* lut_max_kernel_ptr(int Q) {
+    return Q == 4 ? reinterpret_cast<const void*>(&vk::lut_max_kernel<4>)
+                  : reinterpret_cast<const void*>(&vk::lut_max_kernel<8>);
+}
+
+const void* lut_h16_kernel_ptr(int Q) {
+    return Q == 4 ? reinterpret_cast<const void*>(&vk::lut_h16_kernel<4>)
+                  : reinterpret_cast<const void*>(&vk::lut_h16_kernel<8>);
 }
 
 const void* lut_kernel_ptr(int Q) {
@@ -165,6 +183,8 @@ struct vk_index {
     DevBuf<uint32_t> bound;  // per-query running bound of the k-th distance (pruned scan)
     DevBuf<int2> glist;      // per-query global best-k list (pruned scan)
     DevBuf<int> glock;       // per-query try-locks of glist
+    DevBuf<uint32_t> qmax;   // per-query largest LUT entry (half-precision LUTs)
+    DevBuf<int> qexp;        // per-query scale exponent (half-precision LUTs)
     int* flags = nullptr;  // [0] work counter, [1] kernel status word
     cudaEvent_t ev[6] = {};
     int sm_count = 0, smem_optin = 0, clock_khz = 0;
@@ -190,7 +210,7 @@ namespace {
 
 struct Plan {
     int Q = 1, ilp = 1, stages = kStagesMax, S = 1, mt = 0, merge_slots = 1;
-    bool prune = false;
+    bool prune = false, h16 = false, ivf = false;
     int threads = 0, blocks_per_sm = 0, grid = 0;
     int groups = 0, chunks = 0;
     int64_t chunk_len = 0, first_len = 0;
@@ -201,40 +221,56 @@ struct Plan {
 // Chooses Q (the requested queries per block, halved until the LUTs fit, and never more than the batch needs),
 // ILP and the ring depth, then the chunk count with a wave model over the occupancy API's resident blocks:
 // time ~ ceil(items / resident) * (rows per chunk + a LUT-load overhead), minimised over the chunk count.
-int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan& p) {
+// ivf: a plan for IVF work items (Q in {4, 8}, m in {16, 32}, ILP <= 2, fp32 LUTs; no chunking: the items are the
+// (list, query batch) pairs the IVF planning kernels produce).
+int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan& p, bool ivf = false) {
     p.S = s_for_k(k);
     p.mt = (ix->m == 16 || ix->m == 32 || ix->m == 64) ? ix->m : 0;
     // Exact early abandoning: specialised for m in {16, 32, 64}; its compaction queue holds 1 or 2 row groups.
     p.prune = t.early_abandon != 0 && p.mt != 0;
+    p.h16 = t.lut_precision == VK_LUT_F16;
+    p.ivf = ivf;
+    if (p.h16 && p.mt == 0)
+        return fail(VK_ERR_UNSUPPORTED, "half-precision LUTs need m = 16, 32 or 64 (m = %d)", ix->m);
+    if (ivf && (p.h16 || (ix->m != 16 && ix->m != 32)))
+        return fail(VK_ERR_UNSUPPORTED, "IVF search supports m = 16 or 32 with fp32 LUTs (m = %d)", ix->m);
     int Q = t.queries_per_block;
     int64_t need = 1;
     while (need < nq && need < 8) need *= 2;
     Q = (int)std::min<int64_t>(Q, need);
-    const int ilp_req = p.prune ? std::min(t.vectors_per_step, 2) : t.vectors_per_step;
+    if (p.h16) Q = Q >= 8 ? 8 : 4;  // half LUT entries hold 4 or 8 queries
+    if (ivf) Q = Q >= 8 ? 8 : 4;    // IVF items hold 4 or 8 queries
+    const int ilp_req = (p.prune || p.h16 || ivf) ? std::min(t.vectors_per_step, 2) : t.vectors_per_step;
     p.ilp = ilp_req;
     p.stages = kStagesMax;
     // warps per block as the kernel is instantiated (vk::scan_warps); the generic-m kernel uses its table size
-    auto warps = [&](int q) { return vk::scan_warps(q, p.mt); };
+    auto warps = [&](int q) { return vk::scan_warps(q, p.mt, p.h16); };
     auto slots = [&](int q) { return (uint32_t)q * warps(q) * k * 8u <= 16384u ? q : 1; };  // parallel merges
     auto fits = [&](int q, int ilp, int st) {
-        return vk::scan_smem_plan(q, ix->m, ix->W, ilp, warps(q), st, k, p.prune, slots(q)).total <=
+        return vk::scan_smem_plan(q, ix->m, ix->W, ilp, warps(q), st, k, p.prune, slots(q), p.h16, p.ivf).total <=
                (uint32_t)ix->smem_optin;
     };
     for (;;) {
         if (fits(Q, p.ilp, p.stages)) break;
         if (p.stages > 2) { --p.stages; continue; }
         if (p.ilp > 1) { p.ilp /= 2; p.stages = kStagesMax; continue; }
-        if (Q > 1) { Q /= 2; p.ilp = ilp_req; p.stages = kStagesMax; continue; }
+        if (Q > (p.h16 || p.ivf ? 4 : 1)) { Q /= 2; p.ilp = ilp_req; p.stages = kStagesMax; continue; }
         return fail(VK_ERR_INVALID, "LUT does not fit in shared memory (m = %d needs %u bytes, device allows %d)",
-                    ix->m, vk::scan_smem_plan(1, ix->m, ix->W, 1, warps(1), 2, k, p.prune, 1).total, ix->smem_optin);
+                    ix->m, vk::scan_smem_plan(p.h16 ? 4 : 1, ix->m, ix->W, 1, warps(p.h16 ? 4 : 1), 2, k, p.prune, 1,
+                                              p.h16).total,
+                    ix->smem_optin);
     }
     p.Q = Q;
     const int nw = warps(Q);
     p.threads = nw * 32;
-    p.fn = scan_kernel_ptr(Q, p.mt, p.ilp, p.S, p.prune);
+    if (ivf)
+        p.fn = Q == 8 ? vk::scan_kernel_ivf_for<8>(p.mt, p.ilp, p.S, p.prune)
+                      : vk::scan_kernel_ivf_for<4>(p.mt, p.ilp, p.S, p.prune);
+    else
+        p.fn = scan_kernel_ptr(Q, p.mt, p.ilp, p.S, p.prune, p.h16);
     if (!p.fn) return fail(VK_ERR_UNSUPPORTED, "no scan kernel for Q=%d m=%d ilp=%d", Q, ix->m, p.ilp);
     p.merge_slots = slots(Q);
-    p.smem = vk::scan_smem_plan(Q, ix->m, ix->W, p.ilp, nw, p.stages, k, p.prune, p.merge_slots).total;
+    p.smem = vk::scan_smem_plan(Q, ix->m, ix->W, p.ilp, nw, p.stages, k, p.prune, p.merge_slots, p.h16, p.ivf).total;
     auto granted = ix->smem_granted.find(p.fn);
     if (granted == ix->smem_granted.end() || granted->second < p.smem) {
         VK_TRY_CUDA(cudaFuncSetAttribute(p.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
@@ -251,6 +287,12 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     }
     p.blocks_per_sm = std::max(per_sm, 1);
     const int64_t resident = (int64_t)p.blocks_per_sm * ix->sm_count;
+    if (ivf) {  // persistent grid over the item table; the item count is known on the device only
+        p.groups = 1;
+        p.chunks = 1;
+        p.grid = (int)resident;
+        return VK_OK;
+    }
 
     p.groups = (int)ceil_div(nq, Q);
     const int64_t tile_rows = 32 * p.ilp;
@@ -315,6 +357,8 @@ int validate_tuning(const vk_tuning_t* t) {
     if (!(t->vectors_per_step == 1 || t->vectors_per_step == 2 || t->vectors_per_step == 4))
         return fail(VK_ERR_INVALID, "vectors_per_step must be 1, 2 or 4");
     if (t->early_abandon != 0 && t->early_abandon != 1) return fail(VK_ERR_INVALID, "early_abandon must be 0 or 1");
+    if (t->lut_precision != VK_LUT_F32 && t->lut_precision != VK_LUT_F16)
+        return fail(VK_ERR_INVALID, "lut_precision must be VK_LUT_F32 (0) or VK_LUT_F16 (1)");
     return VK_OK;
 }
 
@@ -327,47 +371,91 @@ int check_variant(const vk_index* ix, int variant) {
     return VK_OK;
 }
 
-// Launches LUT -> scan -> merge for one batch of device-resident queries into d_out (nq x k).
-int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk_tuning_t& t, int2* d_out,
-               cudaStream_t st, vk_launch_shape_t* shape, cudaEvent_t* marks) {
-    Plan p;
-    VK_TRY(plan_scan(ix, nq, k, t, p));
-    const int64_t lut_floats = (int64_t)p.groups * p.Q * ix->m * vk::KSUB;
-    VK_TRY(ix->lut.ensure(lut_floats));
-    VK_TRY(ix->part.ensure((size_t)nq * p.chunks * k));
-    VK_TRY(ix->bound.ensure((size_t)nq));
-    VK_TRY(ix->glist.ensure((size_t)nq * k));
-    VK_TRY(ix->glock.ensure((size_t)nq));
+// Device working memory of one search: from the index's buffers (run_search) or carved from the fixed array of
+// vk_search_noalloc.
+struct Workspace {
+    void* lut = nullptr;        // groups x Q x m x 256 entries (fp32, or half for half-precision LUTs)
+    int2* part = nullptr;       // [nq][chunks][k] per-item lists
+    uint32_t* bound = nullptr;  // [nq] pruning bounds
+    int2* glist = nullptr;      // [nq][k] pruning global lists
+    int* glock = nullptr;       // [nq] try-locks
+    int* flags = nullptr;       // [0] work counter, [1] status word
+    uint32_t* qmax = nullptr;   // [nq] half LUTs: largest entry per query
+    int* qexp = nullptr;        // [nq] half LUTs: scale exponent per query
+    // cooperative sharded search (vk_search_device_coop): exchange arrays and the search's epoch
+    unsigned long long* xb = nullptr;
+    unsigned long long* xpeer[vk::COOP_MAX_PEERS] = {};
+    int npeers = 0;
+    uint32_t epoch = 0;
+};
 
+// Bytes each workspace array needs for a plan (the flags are not included).
+struct WorkspaceBytes {
+    size_t lut, part, bound, glist, glock, qmax, qexp;
+};
+WorkspaceBytes workspace_bytes(const vk_index* ix, int64_t nq, int k, const Plan& p) {
+    WorkspaceBytes b;
+    b.lut = (size_t)p.groups * p.Q * ix->m * vk::KSUB * (p.h16 ? 2 : 4);
+    b.part = (size_t)nq * p.chunks * k * sizeof(int2);
+    b.bound = (size_t)nq * sizeof(uint32_t);
+    b.glist = (size_t)nq * k * sizeof(int2);
+    b.glock = (size_t)nq * sizeof(int);
+    b.qmax = p.h16 ? (size_t)nq * sizeof(uint32_t) : 0;
+    b.qexp = p.h16 ? (size_t)nq * sizeof(int) : 0;
+    return b;
+}
+
+// Launches LUT (two passes for half LUTs) -> scan -> merge for one batch of device-resident queries into d_out
+// (nq x k). Resets the work counter; the status word accumulates until it is read.
+int launch_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const Plan& p, const Workspace& w,
+                  int2* d_out, cudaStream_t st, cudaEvent_t* marks) {
     // LUT
     {
-        const void* fn = lut_kernel_ptr(p.Q);
         const size_t smem = (size_t)p.Q * ix->dsub * sizeof(float);
-        if (smem > 48 * 1024) VK_TRY_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         const float* cen = ix->centroids;
-        float* lut = ix->lut.ptr;
-        uint32_t* bound = p.prune ? ix->bound.ptr : nullptr;
-        int2* glist = ix->glist.ptr;
-        int* glock = ix->glock.ptr;
+        uint32_t* bound = p.prune ? w.bound : nullptr;
+        int2* glist = w.glist;
+        int* glock = w.glock;
         int m = ix->m, dsub = ix->dsub, kk = k;
-        void* args[] = {(void*)&cen, (void*)&d_queries, (void*)&nq, (void*)&m, (void*)&dsub, (void*)&lut,
-                        (void*)&bound, (void*)&glist, (void*)&glock, (void*)&kk};
-        VK_TRY_CUDA(cudaLaunchKernel(fn, dim3(ix->m, p.groups), dim3(vk::KSUB), args, smem, st));
+        void* lut = w.lut;
+        if (p.h16) {
+            uint32_t* qmax = w.qmax;
+            int* qexp = w.qexp;
+            const void* fmax = lut_max_kernel_ptr(p.Q);
+            const void* fh = lut_h16_kernel_ptr(p.Q);
+            if (smem > 48 * 1024) {
+                VK_TRY_CUDA(cudaFuncSetAttribute(fmax, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+                VK_TRY_CUDA(cudaFuncSetAttribute(fh, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            }
+            VK_TRY_CUDA(cudaMemsetAsync(qmax, 0, (size_t)nq * sizeof(uint32_t), st));
+            void* a0[] = {(void*)&cen, (void*)&d_queries, (void*)&nq, (void*)&m, (void*)&dsub, (void*)&qmax};
+            VK_TRY_CUDA(cudaLaunchKernel(fmax, dim3(ix->m, p.groups), dim3(vk::KSUB), a0, smem, st));
+            void* a1[] = {(void*)&cen,  (void*)&d_queries, (void*)&nq,    (void*)&m,     (void*)&dsub, (void*)&qmax,
+                          (void*)&qexp, (void*)&lut,       (void*)&bound, (void*)&glist, (void*)&glock, (void*)&kk};
+            VK_TRY_CUDA(cudaLaunchKernel(fh, dim3(ix->m, p.groups), dim3(vk::KSUB), a1, smem, st));
+        } else {
+            const void* fn = lut_kernel_ptr(p.Q);
+            if (smem > 48 * 1024)
+                VK_TRY_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            void* args[] = {(void*)&cen, (void*)&d_queries, (void*)&nq, (void*)&m, (void*)&dsub, (void*)&lut,
+                            (void*)&bound, (void*)&glist, (void*)&glock, (void*)&kk};
+            VK_TRY_CUDA(cudaLaunchKernel(fn, dim3(ix->m, p.groups), dim3(vk::KSUB), args, smem, st));
+        }
     }
     if (marks) VK_TRY_CUDA(cudaEventRecord(marks[0], st));
     // fused scan + top-k
     {
-        VK_TRY_CUDA(cudaMemsetAsync(ix->flags, 0, sizeof(int), st));
+        VK_TRY_CUDA(cudaMemsetAsync(w.flags, 0, sizeof(int), st));
         vk::ScanArgs a{};
         a.codes = ix->codes;
         a.perm = ix->perm;
-        a.lut = ix->lut.ptr;
-        a.part = ix->part.ptr;
-        a.work_counter = ix->flags;
-        a.status = ix->flags + 1;
-        a.bound = ix->bound.ptr;
-        a.glist = ix->glist.ptr;
-        a.glock = ix->glock.ptr;
+        a.lut = static_cast<const float*>(w.lut);
+        a.part = w.part;
+        a.work_counter = w.flags;
+        a.status = w.flags + 1;
+        a.bound = w.bound;
+        a.glist = w.glist;
+        a.glock = w.glock;
         a.n = ix->n;
         a.n_pad = ix->n_pad;
         a.chunk_len = p.chunk_len;
@@ -382,25 +470,65 @@ int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk
         a.stages = p.stages;
         a.merge_slots = p.merge_slots;
         a.wait_budget = ix->wait_budget;
+        a.xb = w.xb;
+        for (int i = 0; i < vk::COOP_MAX_PEERS; ++i) a.xpeer[i] = w.xpeer[i];
+        a.npeers = w.npeers;
+        a.epoch = w.epoch;
         void* args[] = {(void*)&a};
         VK_TRY_CUDA(cudaLaunchKernel(p.fn, dim3(p.grid), dim3(p.threads), args, p.smem, st));
     }
     if (marks) VK_TRY_CUDA(cudaEventRecord(marks[1], st));
     // merge of the per-chunk partial lists: one warp per query, or, when there are fewer queries than SMs and many
-    // lists, one 8-warp block per query
+    // lists, one 8-warp block per query; half LUTs are scaled back to distances here
     {
         const bool wide = nq <= ix->sm_count && (int64_t)p.chunks * k >= 256;
         const void* fn = wide ? merge_wide_kernel_ptr(p.S) : merge_kernel_ptr(p.S);
-        const int2* in = ix->part.ptr;
+        const int2* in = w.part;
+        const int* qexp = p.h16 ? w.qexp : nullptr;
         int lists = p.chunks, k_in = k, kk = k;
         int64_t qstride = (int64_t)p.chunks * k, lstride = k;
         void* args[] = {(void*)&in, (void*)&nq, (void*)&lists, (void*)&k_in, (void*)&qstride, (void*)&lstride,
-                        (void*)&kk, (void*)&d_out};
+                        (void*)&kk, (void*)&d_out, (void*)&qexp};
         if (wide)
             VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)nq), dim3(256), args, 0, st));
         else
             VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)ceil_div(nq, 4)), dim3(128), args, 0, st));
     }
+    return VK_OK;
+}
+
+// One batch of device-resident queries into d_out (nq x k), with the index's own (growing) buffers; `coop`
+// (optional) carries a cooperative search's exchange arrays and epoch.
+int run_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const vk_tuning_t& t, int2* d_out,
+               cudaStream_t st, vk_launch_shape_t* shape, cudaEvent_t* marks, const Workspace* coop = nullptr) {
+    Plan p;
+    VK_TRY(plan_scan(ix, nq, k, t, p));
+    const WorkspaceBytes b = workspace_bytes(ix, nq, k, p);
+    VK_TRY(ix->lut.ensure((b.lut + sizeof(float) - 1) / sizeof(float)));
+    VK_TRY(ix->part.ensure(b.part / sizeof(int2)));
+    VK_TRY(ix->bound.ensure(b.bound / sizeof(uint32_t)));
+    VK_TRY(ix->glist.ensure(b.glist / sizeof(int2)));
+    VK_TRY(ix->glock.ensure(b.glock / sizeof(int)));
+    if (p.h16) {
+        VK_TRY(ix->qmax.ensure(b.qmax / sizeof(uint32_t)));
+        VK_TRY(ix->qexp.ensure(b.qexp / sizeof(int)));
+    }
+    Workspace w;
+    w.lut = ix->lut.ptr;
+    w.part = ix->part.ptr;
+    w.bound = ix->bound.ptr;
+    w.glist = ix->glist.ptr;
+    w.glock = ix->glock.ptr;
+    w.flags = ix->flags;
+    w.qmax = ix->qmax.ptr;
+    w.qexp = ix->qexp.ptr;
+    if (coop) {
+        w.xb = coop->xb;
+        for (int i = 0; i < vk::COOP_MAX_PEERS; ++i) w.xpeer[i] = coop->xpeer[i];
+        w.npeers = coop->npeers;
+        w.epoch = coop->epoch;
+    }
+    VK_TRY(launch_search(ix, d_queries, nq, k, p, w, d_out, st, marks));
     if (shape) {
         shape->threads = p.threads;
         shape->blocks_x = p.chunks;
@@ -554,6 +682,7 @@ void vk_tuning_default(vk_tuning_t* t) {
     t->queries_per_block = 2;
     t->vectors_per_step = 4;
     t->early_abandon = 1;
+    t->lut_precision = VK_LUT_F32;
 }
 
 int vk_tuning_validate(const vk_tuning_t* t) {
@@ -1088,6 +1217,162 @@ int vk_search_device(vk_index_t* ix, const float* d_queries, int64_t nq, int k, 
                       nullptr, nullptr);
 }
 
+// ------------------------------------------------------------------------------------------------ cooperative search
+}  // extern "C"
+
+struct vk_coop {
+    int device = 0;
+    int64_t nq_max = 0;
+    int64_t nq_limit = 0;                       // the smallest nq_max of this shard and the attached ones
+    unsigned long long* xb = nullptr;           // this shard's exchange array (cudaMalloc'd, zeroed)
+    std::vector<unsigned long long*> peers;     // the other shards' arrays
+    std::vector<void*> ipc_opened;              // of those, the ones mapped with cudaIpcOpenMemHandle
+    ~vk_coop() {
+        DeviceGuard g(device);
+        for (void* p : ipc_opened) cudaIpcCloseMemHandle(p);
+        if (xb) cudaFree(xb);
+    }
+};
+
+extern "C" {
+
+int vk_coop_create(int device, int64_t nq_max, vk_coop_t** out) {
+    if (!out) return fail(VK_ERR_INVALID, "out must not be NULL");
+    *out = nullptr;
+    if (nq_max < 1) return fail(VK_ERR_INVALID, "nq_max must be >= 1");
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(guard.err));
+    auto* c = new vk_coop();
+    c->device = device;
+    c->nq_max = nq_max;
+    c->nq_limit = nq_max;
+    cudaError_t e = cudaMalloc(&c->xb, (size_t)nq_max * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(c->xb, 0, (size_t)nq_max * sizeof(unsigned long long));
+    if (e != cudaSuccess) {
+        delete c;
+        return fail(e == cudaErrorMemoryAllocation ? VK_ERR_NOMEM : VK_ERR_CUDA, "cooperative search buffer: %s",
+                    cudaGetErrorString(e));
+    }
+    *out = c;
+    return VK_OK;
+}
+
+// What one shard publishes for the others: its array's IPC handle, the array's length and its device ordinal.
+struct CoopHandle {
+    cudaIpcMemHandle_t ipc;
+    int64_t nq_max;
+    int32_t device;
+    int32_t reserved;
+};
+static_assert(sizeof(CoopHandle) == VK_COOP_HANDLE_BYTES, "VK_COOP_HANDLE_BYTES");
+
+// Posted atomics into another GPU's memory need a link that carries them natively (NVLink); refuse otherwise.
+int check_peer_atomics(int dev, int peer) {
+    if (dev == peer) return VK_OK;
+    int atomics = 0, access = 0;
+    VK_TRY_CUDA(cudaDeviceCanAccessPeer(&access, dev, peer));
+    VK_TRY_CUDA(cudaDeviceGetP2PAttribute(&atomics, cudaDevP2PAttrNativeAtomicSupported, dev, peer));
+    if (!access || !atomics)
+        return fail(VK_ERR_UNSUPPORTED, "device %d cannot make atomic writes into device %d's memory", dev, peer);
+    return VK_OK;
+}
+
+int vk_coop_ipc_handle(const vk_coop_t* c, void* handle) {
+    if (!c || !handle) return fail(VK_ERR_INVALID, "coop and handle must not be NULL");
+    DeviceGuard guard(c->device);
+    CoopHandle h{};
+    VK_TRY_CUDA(cudaIpcGetMemHandle(&h.ipc, c->xb));
+    h.nq_max = c->nq_max;
+    h.device = c->device;
+    std::memcpy(handle, &h, sizeof(h));
+    return VK_OK;
+}
+
+int vk_coop_attach_ipc(vk_coop_t* c, int n, const void* handles) {
+    if (!c || (n > 0 && !handles)) return fail(VK_ERR_INVALID, "coop and handles must not be NULL");
+    if (!c->peers.empty()) return fail(VK_ERR_INVALID, "this cooperative search is already attached");
+    CoopHandle own;
+    VK_TRY(vk_coop_ipc_handle(c, &own));
+    int count = 0;
+    VK_TRY_CUDA(cudaGetDeviceCount(&count));
+    DeviceGuard guard(c->device);
+    for (int i = 0; i < n; ++i) {
+        CoopHandle h;
+        std::memcpy(&h, static_cast<const unsigned char*>(handles) + (size_t)i * VK_COOP_HANDLE_BYTES, sizeof(h));
+        if (std::memcmp(&h.ipc, &own.ipc, sizeof(h.ipc)) == 0) continue;  // this shard's own array
+        if ((int)c->peers.size() >= vk::COOP_MAX_PEERS)
+            return fail(VK_ERR_UNSUPPORTED, "at most %d other shards", vk::COOP_MAX_PEERS);
+        if (h.nq_max < 1 || h.device < 0 || h.device >= count)
+            return fail(VK_ERR_INVALID, "handle %d is not a cooperative search handle of this node", i);
+        VK_TRY(check_peer_atomics(c->device, h.device));
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h.ipc, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return fail(VK_ERR_CUDA, "cudaIpcOpenMemHandle (shard %d): %s", i, cudaGetErrorString(e));
+        c->ipc_opened.push_back(p);
+        c->peers.push_back(static_cast<unsigned long long*>(p));
+        c->nq_limit = std::min(c->nq_limit, h.nq_max);
+    }
+    return VK_OK;
+}
+
+int vk_coop_attach(vk_coop_t* c, int n, vk_coop_t* const* others) {
+    if (!c || (n > 0 && !others)) return fail(VK_ERR_INVALID, "coop and others must not be NULL");
+    if (!c->peers.empty()) return fail(VK_ERR_INVALID, "this cooperative search is already attached");
+    for (int i = 0; i < n; ++i) {
+        const vk_coop* o = others[i];
+        if (!o) return fail(VK_ERR_INVALID, "shard %d is NULL", i);
+        if (o == c) continue;
+        if ((int)c->peers.size() >= vk::COOP_MAX_PEERS)
+            return fail(VK_ERR_UNSUPPORTED, "at most %d other shards", vk::COOP_MAX_PEERS);
+        if (o->device != c->device) {  // this device's kernels write into the other device's memory
+            VK_TRY(check_peer_atomics(c->device, o->device));
+            DeviceGuard g(c->device);
+            const cudaError_t e = cudaDeviceEnablePeerAccess(o->device, 0);
+            if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
+                return fail(VK_ERR_CUDA, "peer access %d -> %d: %s", c->device, o->device, cudaGetErrorString(e));
+            cudaGetLastError();
+        }
+        c->peers.push_back(o->xb);
+        c->nq_limit = std::min(c->nq_limit, o->nq_max);
+    }
+    return VK_OK;
+}
+
+int vk_coop_destroy(vk_coop_t* c) {
+    delete c;
+    return VK_OK;
+}
+
+int vk_search_device_coop(vk_index_t* ix, vk_coop_t* c, uint32_t epoch, const float* d_queries, int64_t nq, int k,
+                          const vk_tuning_t* tuning, vk_neighbor_t* d_out, void* stream) {
+    if (!ix || !c) return fail(VK_ERR_INVALID, "index and coop must not be NULL");
+    if (epoch == 0) return fail(VK_ERR_INVALID, "epoch must be >= 1");
+    if (nq > c->nq_limit)  // every shard's array must hold nq queries
+        return fail(VK_ERR_INVALID, "nq %lld exceeds the cooperative search's nq_max %lld (of this or another shard)",
+                    (long long)nq, (long long)c->nq_limit);
+    if (c->device != ix->device) return fail(VK_ERR_INVALID, "coop and index are on different devices");
+    if (k < 1 || k > 128 || (int64_t)k > ix->n) return fail(VK_ERR_INVALID, "k must be in [1, min(128, n)]");
+    if (nq < 0) return fail(VK_ERR_INVALID, "nq must be >= 0");
+    if (nq > 0 && (!d_queries || !d_out)) return fail(VK_ERR_INVALID, "queries and out must not be NULL");
+    if (nq > max_query_batch(ix))
+        return fail(VK_ERR_INVALID, "nq %lld exceeds the device-path batch limit %lld", (long long)nq,
+                    (long long)max_query_batch(ix));
+    vk_tuning_t t;
+    vk_tuning_default(&t);
+    if (tuning) t = *tuning;
+    VK_TRY(validate_tuning(&t));
+    if (nq == 0) return VK_OK;
+    DeviceGuard guard(ix->device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
+    Workspace w;
+    w.xb = c->xb;
+    for (size_t i = 0; i < c->peers.size(); ++i) w.xpeer[i] = c->peers[i];
+    w.npeers = (int)c->peers.size();
+    w.epoch = epoch;
+    return run_search(ix, d_queries, nq, k, t, reinterpret_cast<int2*>(d_out), static_cast<cudaStream_t>(stream),
+                      nullptr, nullptr, &w);
+}
+
 int vk_index_sync(vk_index_t* ix, void* stream) {
     if (!ix) return fail(VK_ERR_INVALID, "index must not be NULL");
     DeviceGuard guard(ix->device);
@@ -1180,9 +1465,9 @@ int vk_merge_topk_device(int device, const vk_neighbor_t* d_in, int64_t nq, int 
     const int2* in = reinterpret_cast<const int2*>(d_in);
     int2* o = reinterpret_cast<int2*>(d_out);
     switch (s_for_k(k)) {
-        case 1: vk::merge_kernel<1><<<(unsigned)ceil_div(nq, 4), 128, 0, st>>>(in, nq, lists, k_in, query_stride, list_stride, k, o); break;
-        case 2: vk::merge_kernel<2><<<(unsigned)ceil_div(nq, 4), 128, 0, st>>>(in, nq, lists, k_in, query_stride, list_stride, k, o); break;
-        default: vk::merge_kernel<4><<<(unsigned)ceil_div(nq, 4), 128, 0, st>>>(in, nq, lists, k_in, query_stride, list_stride, k, o); break;
+        case 1: vk::merge_kernel<1><<<(unsigned)ceil_div(nq, 4), 128, 0, st>>>(in, nq, lists, k_in, query_stride, list_stride, k, o, nullptr); break;
+        case 2: vk::merge_kernel<2><<<(unsigned)ceil_div(nq, 4), 128, 0, st>>>(in, nq, lists, k_in, query_stride, list_stride, k, o, nullptr); break;
+        default: vk::merge_kernel<4><<<(unsigned)ceil_div(nq, 4), 128, 0, st>>>(in, nq, lists, k_in, query_stride, list_stride, k, o, nullptr); break;
     }
     VK_TRY_CUDA(cudaGetLastError());
     return VK_OK;
@@ -1356,86 +1641,368 @@ extern "C" int vk_search_noalloc(vk_index_t* ix, const float* d_queries, int64_t
 
     Plan p;
     VK_TRY(plan_scan(ix, nq, k, t, p));
-    // Carve the array: LUTs | per-chunk lists | bounds | global lists | locks | counter + status.
+    // Carve the array: LUTs | per-chunk lists | bounds | global lists | locks | half-LUT maxima | exponents |
+    // counter + status.
+    const WorkspaceBytes b = workspace_bytes(ix, nq, k, p);
     const size_t o_lut = 0;
-    const size_t o_part = o_lut + align256((size_t)p.groups * p.Q * ix->m * vk::KSUB * sizeof(float));
-    const size_t o_bound = o_part + align256((size_t)nq * p.chunks * k * sizeof(int2));
-    const size_t o_glist = o_bound + align256((size_t)nq * sizeof(uint32_t));
-    const size_t o_glock = o_glist + align256((size_t)nq * k * sizeof(int2));
-    const size_t o_flags = o_glock + align256((size_t)nq * sizeof(int));
+    const size_t o_part = o_lut + align256(b.lut);
+    const size_t o_bound = o_part + align256(b.part);
+    const size_t o_glist = o_bound + align256(b.bound);
+    const size_t o_glock = o_glist + align256(b.glist);
+    const size_t o_qmax = o_glock + align256(b.glock);
+    const size_t o_qexp = o_qmax + align256(b.qmax);
+    const size_t o_flags = o_qexp + align256(b.qexp);
     const size_t need = o_flags + align256(2 * sizeof(int));
     if (need > VK_NOALLOC_SCRATCH_BYTES)
         return fail(VK_ERR_INVALID,
                     "this search needs %zu bytes of working memory; vk_search_noalloc has %zu (search fewer queries "
                     "per call)",
                     need, (size_t)VK_NOALLOC_SCRATCH_BYTES);
-    float* lut = reinterpret_cast<float*>(base + o_lut);
-    int2* part = reinterpret_cast<int2*>(base + o_part);
-    uint32_t* bound = reinterpret_cast<uint32_t*>(base + o_bound);
-    int2* glist = reinterpret_cast<int2*>(base + o_glist);
-    int* glock = reinterpret_cast<int*>(base + o_glock);
-    int* flags = reinterpret_cast<int*>(base + o_flags);
-
-    // The array keeps the previous call's contents: the work counter and the status word start at zero; the LUT
-    // kernel rewrites the LUTs and, for the pruned scan, resets the bounds, global lists and locks.
-    VK_TRY_CUDA(cudaMemsetAsync(flags, 0, 2 * sizeof(int), st));
-    {
-        const void* fn = lut_kernel_ptr(p.Q);
-        const size_t smem = (size_t)p.Q * ix->dsub * sizeof(float);
-        if (smem > 48 * 1024) VK_TRY_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        const float* cen = ix->centroids;
-        uint32_t* bnd = p.prune ? bound : nullptr;
-        int m = ix->m, dsub = ix->dsub, kk = k;
-        void* args[] = {(void*)&cen, (void*)&d_queries, (void*)&nq, (void*)&m, (void*)&dsub, (void*)&lut,
-                        (void*)&bnd, (void*)&glist, (void*)&glock, (void*)&kk};
-        VK_TRY_CUDA(cudaLaunchKernel(fn, dim3(ix->m, p.groups), dim3(vk::KSUB), args, smem, st));
-    }
-    {
-        vk::ScanArgs a{};
-        a.codes = ix->codes;
-        a.perm = ix->perm;
-        a.lut = lut;
-        a.part = part;
-        a.work_counter = flags;
-        a.status = flags + 1;
-        a.bound = bound;
-        a.glist = glist;
-        a.glock = glock;
-        a.n = ix->n;
-        a.n_pad = ix->n_pad;
-        a.chunk_len = p.chunk_len;
-        a.first_len = p.first_len;
-        a.id_base = ix->id_base;
-        a.m = ix->m;
-        a.W = ix->W;
-        a.nq = (int)nq;
-        a.groups = p.groups;
-        a.chunks = p.chunks;
-        a.k = k;
-        a.stages = p.stages;
-        a.merge_slots = p.merge_slots;
-        a.wait_budget = ix->wait_budget;
-        void* args[] = {(void*)&a};
-        VK_TRY_CUDA(cudaLaunchKernel(p.fn, dim3(p.grid), dim3(p.threads), args, p.smem, st));
-    }
-    {
-        // the same merge choice as vk_search_device: one 8-warp block per query for few queries over many lists
-        const bool wide = nq <= ix->sm_count && (int64_t)p.chunks * k >= 256;
-        const void* fn = wide ? merge_wide_kernel_ptr(p.S) : merge_kernel_ptr(p.S);
-        const int2* in = part;
-        int2* o = reinterpret_cast<int2*>(d_out);
-        int lists = p.chunks, k_in = k, kk = k;
-        int64_t qstride = (int64_t)p.chunks * k, lstride = k;
-        void* args[] = {(void*)&in, (void*)&nq, (void*)&lists, (void*)&k_in, (void*)&qstride, (void*)&lstride,
-                        (void*)&kk, (void*)&o};
-        if (wide)
-            VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)nq), dim3(256), args, 0, st));
-        else
-            VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)ceil_div(nq, 4)), dim3(128), args, 0, st));
-    }
+    Workspace w;
+    w.lut = base + o_lut;
+    w.part = reinterpret_cast<int2*>(base + o_part);
+    w.bound = reinterpret_cast<uint32_t*>(base + o_bound);
+    w.glist = reinterpret_cast<int2*>(base + o_glist);
+    w.glock = reinterpret_cast<int*>(base + o_glock);
+    w.qmax = reinterpret_cast<uint32_t*>(base + o_qmax);
+    w.qexp = reinterpret_cast<int*>(base + o_qexp);
+    w.flags = reinterpret_cast<int*>(base + o_flags);
+    int* flags = w.flags;
+    // The array keeps the previous call's contents: the status word starts at zero here, the work counter in
+    // launch_search; the LUT kernels rewrite the LUTs and, for the pruned scan, reset the bounds, global lists
+    // and locks.
+    VK_TRY_CUDA(cudaMemsetAsync(flags + 1, 0, sizeof(int), st));
+    VK_TRY(launch_search(ix, d_queries, nq, k, p, w, reinterpret_cast<int2*>(d_out), st, nullptr));
     int status = 0;
     VK_TRY_CUDA(cudaMemcpyAsync(&status, flags + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
     VK_TRY_CUDA(cudaStreamSynchronize(st));
     if (status != 0) return status_error(status);
     return VK_OK;
 }
+
+// ------------------------------------------------------------------------------------------------ IVF
+// An IVF index: the rows of each list in a contiguous, 64-aligned range of slots of an ordinary index (its lane
+// placement then never mixes lists), the id of the row in each slot (-1 for padding), and the coarse centroids.
+struct vk_ivf {
+    vk_index* index = nullptr;
+    int device = 0, nlist = 0, d = 0;
+    int64_t n = 0;
+    float* coarse = nullptr;      // [nlist][d]
+    int64_t* list_off = nullptr;  // [nlist]
+    int* list_rows = nullptr;     // [nlist]
+    int32_t* ids = nullptr;       // [index->n_pad]
+    DevBuf<float> queries;
+    DevBuf<int2> out, by_list, item_pairs, part;
+    DevBuf<int32_t> probes;
+    DevBuf<int> counts, item_off, item_list, nitems;
+    DevBuf<int64_t> pair_off;
+    ~vk_ivf() {
+        DeviceGuard g(device);
+        queries.release();
+        out.release();
+        by_list.release();
+        item_pairs.release();
+        part.release();
+        probes.release();
+        counts.release();
+        item_off.release();
+        item_list.release();
+        nitems.release();
+        pair_off.release();
+        if (coarse) cudaFree(coarse);
+        if (list_off) cudaFree(list_off);
+        if (list_rows) cudaFree(list_rows);
+        if (ids) cudaFree(ids);
+        delete index;
+    }
+};
+
+namespace {
+
+constexpr int kIvfMaxProbe = 128;
+
+int64_t ivf_max_items(int64_t nq, int nprobe, int Q, int nlist) {
+    return std::min<int64_t>(nq * nprobe, ceil_div(nq * nprobe, Q) + nlist);
+}
+
+// Largest query batch whose per-item LUTs stay within the LUT budget (at Q = 8, the larger case).
+int64_t ivf_max_batch(const vk_ivf* ivf, int nprobe) {
+    const int64_t lut_item = (int64_t)8 * ivf->index->m * vk::KSUB * 4;
+    const int64_t items = std::max<int64_t>(1, std::min<int64_t>(65535, (int64_t)(kLutBudgetBytes / lut_item)) - ivf->nlist);
+    return std::max<int64_t>(1, std::min<int64_t>(items * 4 / nprobe, 1 << 20));
+}
+
+// Probe selection, planning, per-item LUTs, the IVF scan and the merge of each query's nprobe lists into d_out.
+int ivf_run(vk_ivf* ivf, const float* d_queries, int64_t nq, int k, int nprobe, const vk_tuning_t& t, int2* d_out,
+            cudaStream_t st) {
+    vk_index* ix = ivf->index;
+    Plan p;
+    VK_TRY(plan_scan(ix, nq, k, t, p, true));
+    const int Q = p.Q, nlist = ivf->nlist;
+    const int64_t pairs = nq * nprobe;
+    const int64_t max_items = ivf_max_items(nq, nprobe, Q, nlist);
+    if (max_items > 65535)  // one LUT block row per item (grid.y)
+        return fail(VK_ERR_INVALID, "too many (query, list) pairs in one IVF batch (%lld work items)",
+                    (long long)max_items);
+    VK_TRY(ix->lut.ensure((size_t)max_items * Q * ix->m * vk::KSUB));
+    VK_TRY(ix->bound.ensure((size_t)nq));
+    VK_TRY(ix->glist.ensure((size_t)nq * k));
+    VK_TRY(ix->glock.ensure((size_t)nq));
+    VK_TRY(ivf->probes.ensure((size_t)pairs));
+    VK_TRY(ivf->counts.ensure((size_t)2 * nlist));
+    VK_TRY(ivf->pair_off.ensure((size_t)nlist + 1));
+    VK_TRY(ivf->item_off.ensure((size_t)nlist + 1));
+    VK_TRY(ivf->nitems.ensure(1));
+    VK_TRY(ivf->by_list.ensure((size_t)pairs));
+    VK_TRY(ivf->item_list.ensure((size_t)max_items));
+    VK_TRY(ivf->item_pairs.ensure((size_t)max_items * Q));
+    VK_TRY(ivf->part.ensure((size_t)pairs * k));
+    const unsigned pgrid = grid_for(pairs, ix->sm_count);
+    switch (s_for_k(nprobe)) {
+        case 1: vk::ivf_probe_kernel<1><<<(unsigned)ceil_div(nq, 4), 128, 0, st>>>(d_queries, nq, ivf->d, ivf->coarse, nlist, nprobe, ivf->probes.ptr, ix->bound.ptr, ix->glist.ptr, ix->glock.ptr, k); break;
+        case 2: vk::ivf_probe_kernel<2><<<(unsigned)ceil_div(nq, 4), 128, 0, st>>>(d_queries, nq, ivf->d, ivf->coarse, nlist, nprobe, ivf->probes.ptr, ix->bound.ptr, ix->glist.ptr, ix->glock.ptr, k); break;
+        default: vk::ivf_probe_kernel<4><<<(unsigned)ceil_div(nq, 4), 128, 0, st>>>(d_queries, nq, ivf->d, ivf->coarse, nlist, nprobe, ivf->probes.ptr, ix->bound.ptr, ix->glist.ptr, ix->glock.ptr, k); break;
+    }
+    VK_TRY_CUDA(cudaGetLastError());
+    VK_TRY_CUDA(cudaMemsetAsync(ivf->counts.ptr, 0, (size_t)2 * nlist * sizeof(int), st));
+    vk::ivf_count_kernel<<<pgrid, 256, 0, st>>>(ivf->probes.ptr, pairs, ivf->counts.ptr);
+    vk::ivf_plan_kernel<<<1, 1024, 0, st>>>(ivf->counts.ptr, nlist, Q, ivf->pair_off.ptr, ivf->item_off.ptr,
+                                           ivf->nitems.ptr);
+    vk::ivf_fill_kernel<<<pgrid, 256, 0, st>>>(ivf->probes.ptr, nq, nprobe, ivf->pair_off.ptr, ivf->counts.ptr + nlist,
+                                              ivf->by_list.ptr);
+    vk::ivf_items_kernel<<<(unsigned)std::min<int64_t>(nlist, (int64_t)ix->sm_count * 8), 256, 0, st>>>(
+        ivf->pair_off.ptr, ivf->item_off.ptr, nlist, Q, ivf->by_list.ptr, ivf->item_list.ptr, ivf->item_pairs.ptr);
+    VK_TRY_CUDA(cudaGetLastError());
+    {
+        const size_t smem = (size_t)Q * ix->dsub * sizeof(float);
+        const void* fn = Q == 8 ? reinterpret_cast<const void*>(&vk::ivf_lut_kernel<8>)
+                                : reinterpret_cast<const void*>(&vk::ivf_lut_kernel<4>);
+        if (smem > 48 * 1024) VK_TRY_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        const float* cen = ix->centroids;
+        const int2* pp = ivf->item_pairs.ptr;
+        const int* ni = ivf->nitems.ptr;
+        float* lut = ix->lut.ptr;
+        int m = ix->m, dsub = ix->dsub;
+        void* args[] = {(void*)&cen, (void*)&d_queries, (void*)&nq, (void*)&m, (void*)&dsub, (void*)&pp, (void*)&ni,
+                        (void*)&lut};
+        VK_TRY_CUDA(cudaLaunchKernel(fn, dim3(ix->m, (unsigned)max_items), dim3(vk::KSUB), args, smem, st));
+    }
+    {
+        VK_TRY_CUDA(cudaMemsetAsync(ix->flags, 0, sizeof(int), st));
+        vk::ScanArgs a{};
+        a.codes = ix->codes;
+        a.perm = ix->perm;
+        a.lut = ix->lut.ptr;
+        a.part = ivf->part.ptr;
+        a.work_counter = ix->flags;
+        a.status = ix->flags + 1;
+        a.bound = ix->bound.ptr;
+        a.glist = ix->glist.ptr;
+        a.glock = ix->glock.ptr;
+        a.n = ix->n;
+        a.n_pad = ix->n_pad;
+        a.chunk_len = ix->n_pad;
+        a.first_len = ix->n_pad;
+        a.id_base = 0;
+        a.m = ix->m;
+        a.W = ix->W;
+        a.nq = (int)nq;
+        a.groups = 1;
+        a.chunks = 1;
+        a.k = k;
+        a.stages = p.stages;
+        a.merge_slots = p.merge_slots;
+        a.wait_budget = ix->wait_budget;
+        a.ivf_item_list = ivf->item_list.ptr;
+        a.ivf_item_pairs = ivf->item_pairs.ptr;
+        a.ivf_list_off = ivf->list_off;
+        a.ivf_list_rows = ivf->list_rows;
+        a.ivf_ids = ivf->ids;
+        a.ivf_nitems = ivf->nitems.ptr;
+        a.nprobe = nprobe;
+        void* args[] = {(void*)&a};
+        VK_TRY_CUDA(cudaLaunchKernel(p.fn, dim3(p.grid), dim3(p.threads), args, p.smem, st));
+    }
+    {
+        const bool wide = nq <= ix->sm_count && (int64_t)nprobe * k >= 256;
+        const void* fn = wide ? merge_wide_kernel_ptr(p.S) : merge_kernel_ptr(p.S);
+        const int2* in = ivf->part.ptr;
+        const int* qexp = nullptr;
+        int lists = nprobe, k_in = k, kk = k;
+        int64_t qstride = (int64_t)nprobe * k, lstride = k;
+        void* args[] = {(void*)&in, (void*)&nq, (void*)&lists, (void*)&k_in, (void*)&qstride, (void*)&lstride,
+                        (void*)&kk, (void*)&d_out, (void*)&qexp};
+        if (wide)
+            VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)nq), dim3(256), args, 0, st));
+        else
+            VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)ceil_div(nq, 4)), dim3(128), args, 0, st));
+    }
+    return VK_OK;
+}
+
+int ivf_check(const vk_ivf* ivf, int64_t nq, int k, int nprobe) {
+    if (!ivf) return fail(VK_ERR_INVALID, "IVF index must not be NULL");
+    if (k < 1 || k > 128) return fail(VK_ERR_INVALID, "k must be in [1, 128]");
+    if (nprobe < 1 || nprobe > std::min(kIvfMaxProbe, ivf->nlist))
+        return fail(VK_ERR_INVALID, "nprobe must be in [1, min(128, nlist)]");
+    if (nq < 0) return fail(VK_ERR_INVALID, "nq must be >= 0");
+    return VK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int vk_ivf_create(int device, const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
+                  const float* coarse, int nlist, const int32_t* list_of, vk_ivf_t** out) {
+    if (!out) return fail(VK_ERR_INVALID, "out must not be NULL");
+    *out = nullptr;
+    if (!centroids || !codes || !coarse || !list_of) return fail(VK_ERR_INVALID, "pointers must not be NULL");
+    if (m <= 0 || dsub <= 0 || n <= 0 || nlist <= 0) return fail(VK_ERR_INVALID, "bad sizes");
+    if (n >= (int64_t)std::numeric_limits<int>::max()) return fail(VK_ERR_INVALID, "n must fit in int32 ids");
+    std::vector<int64_t> cnt((size_t)nlist, 0);
+    for (int64_t i = 0; i < n; ++i) {
+        if (list_of[i] < 0 || list_of[i] >= nlist) return fail(VK_ERR_INVALID, "row %lld has list %d outside [0, %d)",
+                                                                (long long)i, list_of[i], nlist);
+        ++cnt[(size_t)list_of[i]];
+    }
+    // 64-aligned list ranges, rows in id order within a list, padding slots with id -1
+    std::vector<int64_t> off((size_t)nlist);
+    std::vector<int> rows((size_t)nlist);
+    int64_t slots = 0;
+    for (int l = 0; l < nlist; ++l) {
+        off[(size_t)l] = slots;
+        rows[(size_t)l] = (int)(ceil_div(cnt[(size_t)l], vk::PLACE_WINDOW) * vk::PLACE_WINDOW);
+        slots += rows[(size_t)l];
+    }
+    if (slots >= (int64_t)std::numeric_limits<int>::max() - 128) return fail(VK_ERR_INVALID, "too many rows");
+    const int64_t slots_alloc = std::max<int64_t>(slots, vk::PLACE_WINDOW);  // an index needs at least one row
+    std::vector<uint8_t> slot_codes((size_t)slots_alloc * m, 0);
+    std::vector<int32_t> slot_ids((size_t)ceil_div(slots_alloc, 128) * 128, -1);
+    std::vector<int64_t> fill((size_t)nlist, 0);
+    for (int64_t i = 0; i < n; ++i) {
+        const int l = list_of[i];
+        const int64_t pos = off[(size_t)l] + fill[(size_t)l]++;
+        std::memcpy(slot_codes.data() + pos * m, codes + i * m, (size_t)m);
+        slot_ids[(size_t)pos] = (int32_t)i;
+    }
+    auto* ivf = new vk_ivf();
+    ivf->device = device;
+    ivf->nlist = nlist;
+    ivf->d = m * dsub;
+    ivf->n = n;
+    int rc = vk_index_create(device, centroids, m, dsub, slot_codes.data(), slots_alloc, 0, &ivf->index);
+    if (rc == VK_OK) {
+        DeviceGuard guard(device);
+        cudaError_t e = cudaMalloc(&ivf->coarse, (size_t)nlist * ivf->d * sizeof(float));
+        if (e == cudaSuccess) e = cudaMalloc(&ivf->list_off, (size_t)nlist * sizeof(int64_t));
+        if (e == cudaSuccess) e = cudaMalloc(&ivf->list_rows, (size_t)nlist * sizeof(int));
+        if (e == cudaSuccess) e = cudaMalloc(&ivf->ids, (size_t)ivf->index->n_pad * sizeof(int32_t));
+        if (e == cudaSuccess)
+            e = cudaMemcpy(ivf->coarse, coarse, (size_t)nlist * ivf->d * sizeof(float), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(ivf->list_off, off.data(), (size_t)nlist * sizeof(int64_t), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(ivf->list_rows, rows.data(), (size_t)nlist * sizeof(int), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(ivf->ids, slot_ids.data(), (size_t)ivf->index->n_pad * sizeof(int32_t), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) rc = fail(VK_ERR_CUDA, "IVF index build: %s", cudaGetErrorString(e));
+    }
+    if (rc != VK_OK) {
+        delete ivf;
+        return rc;
+    }
+    *out = ivf;
+    return VK_OK;
+}
+
+int vk_ivf_destroy(vk_ivf_t* ivf) {
+    delete ivf;
+    return VK_OK;
+}
+
+int vk_ivf_info(const vk_ivf_t* ivf, int64_t* n, int* nlist, int64_t* slots) {
+    if (!ivf) return fail(VK_ERR_INVALID, "IVF index must not be NULL");
+    if (n) *n = ivf->n;
+    if (nlist) *nlist = ivf->nlist;
+    if (slots) *slots = ivf->index->n;
+    return VK_OK;
+}
+
+int vk_ivf_search_device(vk_ivf_t* ivf, const float* d_queries, int64_t nq, int k, int nprobe,
+                         const vk_tuning_t* tuning, vk_neighbor_t* d_out, void* stream) {
+    VK_TRY(ivf_check(ivf, nq, k, nprobe));
+    if (nq > 0 && (!d_queries || !d_out)) return fail(VK_ERR_INVALID, "queries and out must not be NULL");
+    if (nq > ivf_max_batch(ivf, nprobe))
+        return fail(VK_ERR_INVALID, "nq %lld exceeds the IVF batch limit %lld for nprobe %d", (long long)nq,
+                    (long long)ivf_max_batch(ivf, nprobe), nprobe);
+    vk_tuning_t t;
+    vk_tuning_default(&t);
+    if (tuning) t = *tuning;
+    VK_TRY(validate_tuning(&t));
+    if (nq == 0) return VK_OK;
+    DeviceGuard guard(ivf->device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
+    return ivf_run(ivf, d_queries, nq, k, nprobe, t, reinterpret_cast<int2*>(d_out), static_cast<cudaStream_t>(stream));
+}
+
+int vk_ivf_search(vk_ivf_t* ivf, const float* queries, int64_t nq, int k, int nprobe, const vk_tuning_t* tuning,
+                  vk_neighbor_t* out, vk_timings_t* timings) {
+    VK_TRY(ivf_check(ivf, nq, k, nprobe));
+    if (nq > 0 && (!queries || !out)) return fail(VK_ERR_INVALID, "queries and out must not be NULL");
+    vk_tuning_t t;
+    vk_tuning_default(&t);
+    if (tuning) t = *tuning;
+    VK_TRY(validate_tuning(&t));
+    if (timings) *timings = vk_timings_t{};
+    if (nq == 0) return VK_OK;
+    DeviceGuard guard(ivf->device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
+    vk_index* ix = ivf->index;
+    cudaStream_t st = ix->stream;
+    const int64_t batch = std::min(nq, ivf_max_batch(ivf, nprobe));
+    VK_TRY(ivf->queries.ensure((size_t)batch * ivf->d));
+    VK_TRY(ivf->out.ensure((size_t)batch * k));
+    vk_timings_t acc{};
+    cudaEvent_t* ev = ix->ev;
+    for (int64_t q0 = 0; q0 < nq; q0 += batch) {
+        const int64_t b = std::min(batch, nq - q0);
+        VK_TRY_CUDA(cudaEventRecord(ev[0], st));
+        VK_TRY_CUDA(cudaMemcpyAsync(ivf->queries.ptr, queries + q0 * ivf->d, (size_t)b * ivf->d * sizeof(float),
+                                    cudaMemcpyHostToDevice, st));
+        VK_TRY_CUDA(cudaEventRecord(ev[1], st));
+        VK_TRY(ivf_run(ivf, ivf->queries.ptr, b, k, nprobe, t, ivf->out.ptr, st));
+        VK_TRY_CUDA(cudaEventRecord(ev[2], st));
+        VK_TRY_CUDA(cudaMemcpyAsync(out + q0 * k, ivf->out.ptr, (size_t)b * k * sizeof(int2), cudaMemcpyDeviceToHost, st));
+        VK_TRY_CUDA(cudaEventRecord(ev[3], st));
+        VK_TRY_CUDA(cudaEventSynchronize(ev[3]));
+        float ms[3];
+        for (int i = 0; i < 3; ++i) VK_TRY_CUDA(cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]));
+        acc.transfer_ms += ms[0] + ms[2];
+        acc.scan_ms += ms[1];
+    }
+    VK_TRY(read_status(ix, st));
+    if (timings) *timings = acc;
+    return VK_OK;
+}
+
+int vk_ivf_sync(vk_ivf_t* ivf, void* stream) {
+    if (!ivf) return fail(VK_ERR_INVALID, "IVF index must not be NULL");
+    DeviceGuard guard(ivf->device);
+    return read_status(ivf->index, static_cast<cudaStream_t>(stream));
+}
+
+int vk_ivf_assign_device(int device, const float* d_x, int64_t n, int d, const float* d_coarse, int nlist,
+                         int32_t* d_list_of, void* stream) {
+    if (!d_x || !d_coarse || !d_list_of) return fail(VK_ERR_INVALID, "pointers must not be NULL");
+    if (n < 0 || d <= 0 || nlist <= 0) return fail(VK_ERR_INVALID, "bad sizes");
+    if (n == 0) return VK_OK;
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(guard.err));
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    vk::ivf_assign_kernel<<<grid_for(n, sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(d_x, n, d, d_coarse, nlist,
+                                                                                          d_list_of);
+    VK_TRY_CUDA(cudaGetLastError());
+    return VK_OK;
+}
+
+}  // extern "C"

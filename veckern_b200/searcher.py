@@ -51,10 +51,11 @@ class Tuning:
     queries_per_block: int = 2
     vectors_per_step: int = 4
     early_abandon: bool = True  # exact pruning by partial sums (results identical); False = full scan
+    lut_f16: bool = False       # half-precision LUTs (vk_abi.h VK_LUT_F16: an approximate search, exactly defined)
 
     def c(self) -> N.Tuning:
         return N.Tuning(self.scan_threads, self.blocks_per_query, self.queries_per_block, self.vectors_per_step,
-                        int(self.early_abandon))
+                        int(self.early_abandon), N.VK_LUT_F16 if self.lut_f16 else N.VK_LUT_F32)
 
 
 @dataclass
@@ -224,6 +225,15 @@ class PQSearcher:
         s = _stream_handle(stream)
         check(lib().vk_search_device(self._h, ptr(d_queries), nq, k, C.byref(tun), ptr(d_out), s), "search_device")
 
+    def search_device_coop(self, coop: "CoopSearch", epoch: int, d_queries, k: int, d_out, stream=None,
+                           tuning: Tuning | None = None) -> None:
+        """search_device as one shard of a cooperative sharded search (vk_search_device_coop): the lists are exact
+        only once merged with the other shards' lists of the same epoch."""
+        nq = d_queries.shape[0]
+        tun = (tuning or self.tuning).c()
+        check(lib().vk_search_device_coop(self._h, coop._h, epoch, ptr(d_queries), nq, k, C.byref(tun), ptr(d_out),
+                                          _stream_handle(stream)), "search_device_coop")
+
     def sync(self, stream=None) -> None:
         check(lib().vk_index_sync(self._h, _stream_handle(stream)), "sync")
 
@@ -245,6 +255,120 @@ class PQSearcher:
         out = np.empty(count, np.uint8)
         check(lib().vk_index_get_placement(self._h, 0, count, ptr(out)), "get_placement")
         return out
+
+
+class IVFSearcher:
+    """IVF (inverted-file) PQ search on one GPU (vk_ivf_*, include/vk_abi.h): the flat search restricted to the rows
+    of each query's nprobe nearest lists. list_of: the list of each row (e.g. assign_lists)."""
+
+    def __init__(self, centroids, codes, coarse, list_of, *, device: int = 0):
+        centroids = np.ascontiguousarray(centroids, np.float32)
+        codes = np.ascontiguousarray(codes, np.uint8)
+        coarse = np.ascontiguousarray(coarse, np.float32)
+        list_of = np.ascontiguousarray(list_of, np.int32)
+        m, _, dsub = centroids.shape
+        if codes.ndim != 2 or codes.shape[1] != m or list_of.shape != (codes.shape[0],):
+            raise ValueError("codes must be [n, m] uint8 and list_of [n] int32")
+        if coarse.ndim != 2 or coarse.shape[1] != m * dsub:
+            raise ValueError("coarse must be [nlist, d] float32")
+        self._h = C.c_void_p()
+        check(lib().vk_ivf_create(device, ptr(centroids), m, dsub, ptr(codes), codes.shape[0], ptr(coarse),
+                                  coarse.shape[0], ptr(list_of), C.byref(self._h)), "vk_ivf_create")
+        self.d, self.device, self.nlist, self.n = m * dsub, device, coarse.shape[0], codes.shape[0]
+        self.tuning = Tuning(queries_per_block=8, vectors_per_step=2)
+
+    def set_tuning(self, tuning: Tuning) -> None:
+        t = tuning.c()
+        check(lib().vk_tuning_validate(C.byref(t)), "set_tuning")
+        self.tuning = tuning
+
+    def search(self, queries, k: int, nprobe: int, out: np.ndarray | None = None):
+        """HOST queries [nq, d] -> HOST results [nq, k] (NEIGHBOR_DTYPE). Returns (out, Timings)."""
+        queries = np.ascontiguousarray(queries, np.float32).reshape(-1, self.d)
+        nq = queries.shape[0]
+        if out is None:
+            out = empty_neighbors(nq, k)
+        t, tun = N.Timings(), self.tuning.c()
+        check(lib().vk_ivf_search(self._h, ptr(queries), nq, k, nprobe, C.byref(tun), ptr(out), C.byref(t)),
+              "ivf_search")
+        return out, Timings(t.transfer_ms, t.lut_ms, t.scan_ms, t.select_ms)
+
+    def search_device(self, d_queries, k: int, nprobe: int, d_out, stream=None) -> None:
+        tun = self.tuning.c()
+        check(lib().vk_ivf_search_device(self._h, ptr(d_queries), d_queries.shape[0], k, nprobe, C.byref(tun),
+                                         ptr(d_out), _stream_handle(stream)), "ivf_search_device")
+
+    def sync(self, stream=None) -> None:
+        check(lib().vk_ivf_sync(self._h, _stream_handle(stream)), "ivf_sync")
+
+    def close(self) -> None:
+        if self._h:
+            lib().vk_ivf_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+def assign_lists(x, coarse, device: int = 0) -> np.ndarray:
+    """The nearest coarse centroid of each row of x (vk_ivf_assign_device: exact l2sq, first minimum wins)."""
+    import torch
+
+    coarse = np.ascontiguousarray(coarse, np.float32)
+    with torch.cuda.device(device):
+        dc = torch.from_numpy(coarse).cuda()
+        out = np.empty(x.shape[0], np.int32)
+        step = 1 << 20
+        for a in range(0, x.shape[0], step):
+            xs = torch.from_numpy(np.ascontiguousarray(x[a:a + step], np.float32)).cuda()
+            o = torch.empty(xs.shape[0], dtype=torch.int32, device="cuda")
+            check(lib().vk_ivf_assign_device(device, ptr(xs), xs.shape[0], xs.shape[1], ptr(dc), coarse.shape[0],
+                                             ptr(o), torch.cuda.current_stream().cuda_stream), "ivf_assign")
+            out[a:a + xs.shape[0]] = o.cpu().numpy()
+    return out
+
+
+class CoopSearch:
+    """The pruning-bound exchange of one shard of a cooperative sharded search (vk_coop_*, include/vk_abi.h)."""
+
+    def __init__(self, device: int, nq_max: int):
+        self._h = C.c_void_p()
+        check(lib().vk_coop_create(device, nq_max, C.byref(self._h)), "vk_coop_create")
+
+    def ipc_handle(self) -> bytes:
+        buf = C.create_string_buffer(N.COOP_HANDLE_BYTES)
+        check(lib().vk_coop_ipc_handle(self._h, buf), "vk_coop_ipc_handle")
+        return buf.raw
+
+    def attach_ipc(self, handles) -> None:
+        """Maps the other shards' exchange arrays from their handles (all shards' handles, this one's included)."""
+        blob = b"".join(handles)
+        check(lib().vk_coop_attach_ipc(self._h, len(handles), C.c_char_p(blob)), "vk_coop_attach_ipc")
+
+    def attach(self, coops) -> None:
+        """The same for shards in this process."""
+        arr = (C.c_void_p * len(coops))(*[c._h for c in coops])
+        check(lib().vk_coop_attach(self._h, len(coops), arr), "vk_coop_attach")
+
+    def close(self) -> None:
+        if self._h:
+            lib().vk_coop_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class MultiPQSearcher:
