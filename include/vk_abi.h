@@ -121,6 +121,23 @@ int vk_tuning_validate(const vk_tuning_t* t);
 int vk_index_create(int device, const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
                     int64_t id_base, vk_index_t** out);
 
+/* 4-bit PQ index, the 4-bit codes the reference lists as a next step (README.md:219); no counterpart in its API.
+ * centroids: [m][16][dsub] fp32 (16 centroids per sub-space); codes: HOST, row-major n x (m / 2) bytes, sub-code s
+ * of a row in nibble s % 2 (low nibble first) of byte s / 2; m = 16, 32 or 64 (VK_ERR_UNSUPPORTED otherwise).
+ * vk_search, vk_search_device, vk_search_device_coop and vk_search_noalloc accept the index; fp32 LUTs only.
+ * Definition (restated on the CPU by oracle vko_adc_search_pq4): lut[s][c] = l2sq(query sub-vector s, centroid
+ * (s, c)) for c < 16 with the arithmetic of the 8-bit path; a row's distance is the fp32 sum of lut[s][code_s] over
+ * s = 0..m-1 in order; the k smallest (distance, id) pairs, ties to the lower id, padded with {+inf, -1}.
+ * vk_host_pq4_train / vk_host_pq4_encode (include/vk_host.h) build such codebooks and codes. The index's device
+ * copy interleaves the bytes in 16-byte words (32 sub-codes each) and keeps rows in id order; vk_index_get_codes
+ * returns the packed bytes. vk_distances, vk_compute_lut_device and vk_index_save reject 4-bit indexes
+ * (VK_ERR_UNSUPPORTED). */
+int vk_index_create_pq4(int device, const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
+                        int64_t id_base, vk_index_t** out);
+
+/* Bits per sub-code of an index: 8 or 4. */
+int vk_index_bits(const vk_index_t* index, int* nbits);
+
 /* Same, with the row-major codes already in DEVICE memory of `device` (e.g. produced by vk_encode_device). */
 int vk_index_create_from_device(int device, const float* centroids, int m, int dsub, const uint8_t* d_codes,
                                 int64_t n, int64_t id_base, vk_index_t** out);

@@ -25,6 +25,12 @@ int vk_host_pq_train(const float* x, int64_t n, int d, int m, int64_t iters, uin
 int vk_host_pq_encode(const float* centroids, int d, int m, const float* x, int64_t n, uint8_t* codes);
 int vk_host_pq_decode(const float* centroids, int d, int m, const uint8_t* codes, int64_t n, float* x);
 
+/* 4-bit PQ (no counterpart in the reference, which lists 4-bit codes as a next step, README.md:219): the same
+ * trainer with 16 centroids per sub-space (n >= 16; centroids [m][16][dsub]), and the encoder that packs the first
+ * nearest of the 16 centroids of sub-space s into nibble s % 2 (low first) of byte s / 2 (n x ceil(m / 2) bytes). */
+int vk_host_pq4_train(const float* x, int64_t n, int d, int m, int64_t iters, uint64_t seed, float* centroids);
+int vk_host_pq4_encode(const float* centroids, int d, int m, const float* x, int64_t n, uint8_t* codes);
+
 int vk_host_synthetic_clustered(int64_t n, int d, int64_t clusters, uint64_t seed, float* out);
 
 /* rows [row0, row0 + rows) of d i.i.d. N(0,1) values (Box-Muller on two 53-bit uniforms per value) */

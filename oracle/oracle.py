@@ -53,6 +53,10 @@ class Port:
                                          C.c_int]
         L.vko_ivf_search.argtypes = [_f32p, C.c_int, C.c_int, _u8p, _i32p, _i64, _f32p, C.c_int, _f32p, _i64,
                                      C.c_int, C.c_int, _f32p, _i32p, _i32p, C.c_int]
+        L.vko_pq4_encode.argtypes = [_f32p, C.c_int, C.c_int, _f32p, _i64, _u8p]
+        L.vko_compute_lut_pq4.argtypes = [_f32p, C.c_int, C.c_int, _f32p, _i64, _f32p]
+        L.vko_adc_search_pq4.argtypes = [_f32p, C.c_int, C.c_int, _u8p, _i64, _f32p, _i64, C.c_int, _f32p, _i32p,
+                                         C.c_int]
         L.vko_stream_create.argtypes = [_f32p, _i64, C.c_int, C.c_int]
         L.vko_stream_create.restype = C.c_void_p
         L.vko_stream_feed.argtypes = [C.c_void_p, _u8p, _i64, _i64, C.c_int]
@@ -133,6 +137,35 @@ class Port:
         self.lib.vko_ivf_search(centroids, m, dsub, codes, list_of, codes.shape[0], coarse, coarse.shape[0], queries,
                                 nq, nprobe, k, d, i, probes, threads)
         return d, i, probes
+
+    def pq4_encode(self, centroids, x):
+        """4-bit codes [n, ceil(m / 2)] (first nearest of 16 centroids, sub-code s in nibble s % 2 of byte s / 2)."""
+        centroids = _f32(centroids)
+        m, _, dsub = centroids.shape
+        x = _f32(x).reshape(-1, m * dsub)
+        codes = np.empty((x.shape[0], (m + 1) // 2), np.uint8)
+        self.lib.vko_pq4_encode(centroids, m, dsub, x, x.shape[0], codes)
+        return codes
+
+    def compute_lut_pq4(self, centroids, queries):
+        centroids = _f32(centroids)
+        m, _, dsub = centroids.shape
+        queries = _f32(queries).reshape(-1, m * dsub)
+        lut = np.empty((queries.shape[0], m, 16), np.float32)
+        self.lib.vko_compute_lut_pq4(centroids, m, dsub, queries, queries.shape[0], lut)
+        return lut
+
+    def adc_search_pq4(self, centroids, codes, queries, k, threads=0):
+        """The 4-bit PQ search (centroids [m, 16, dsub], packed codes) -> (dists [nq, k], ids [nq, k])."""
+        centroids = _f32(centroids)
+        m, _, dsub = centroids.shape
+        codes = _u8(codes)
+        queries = _f32(queries).reshape(-1, m * dsub)
+        nq = queries.shape[0]
+        d = np.empty((nq, k), np.float32)
+        i = np.empty((nq, k), np.int32)
+        self.lib.vko_adc_search_pq4(centroids, m, dsub, codes, codes.shape[0], queries, nq, k, d, i, threads)
+        return d, i
 
     def topk_push_all(self, dists, ids, k):
         dists = _f32(dists)

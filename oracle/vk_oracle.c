@@ -309,6 +309,82 @@ void vko_ivf_search(const float* centroids, int m, int dsub, const uint8_t* code
     }
 }
 
+/* ---------------------------------------------------------------- 4-bit PQ
+ * Not in the reference, which lists 4-bit PQ as a next step (README.md:219); this is the definition the library's
+ * 4-bit indexes (vk_index_create_pq4) implement, restated on the CPU. 16 centroids per sub-space ([m][16][dsub]);
+ * sub-code s of a row sits in nibble s % 2 (low first) of byte s / 2 (ceil(m / 2) bytes per row):
+ *   lut[s][c] = l2sq(query sub-vector s, centroid (s, c)) for c < 16 (the arithmetic of compute_lut);
+ *   distance  = fp32 sum over s = 0..m-1 of lut[s][code_s], from 0, in order (adc_scan's order);
+ *   result    = the k smallest (distance, id) pairs (TopK), ascending, padded with {+inf, -1};
+ *   encoding  = the first nearest of the 16 centroids under l2sq (pq.cpp:11-22's rule). */
+#define KSUB4 16
+
+static inline uint32_t nib(const uint8_t* row, int s) { return (row[s >> 1] >> (4 * (s & 1))) & 0xfu; }
+
+void vko_pq4_encode(const float* centroids, int m, int dsub, const float* x, int64_t n, uint8_t* codes) {
+    const int64_t d = (int64_t)m * dsub, mb = (m + 1) / 2;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        uint8_t* row = codes + i * mb;
+        memset(row, 0, (size_t)mb);
+        for (int s = 0; s < m; ++s) {
+            int best = 0;
+            float best_d = 3.402823466e+38f;
+            for (int c = 0; c < KSUB4; ++c) {
+                const float dist = l2sq(x + i * d + (int64_t)s * dsub, centroids + ((int64_t)s * KSUB4 + c) * dsub, dsub);
+                if (dist < best_d) {
+                    best_d = dist;
+                    best = c;
+                }
+            }
+            row[s >> 1] |= (uint8_t)(best << (4 * (s & 1)));
+        }
+    }
+}
+
+void vko_compute_lut_pq4(const float* centroids, int m, int dsub, const float* queries, int64_t nq, float* lut) {
+    const int64_t d = (int64_t)m * dsub;
+#pragma omp parallel for schedule(static)
+    for (int64_t q = 0; q < nq; ++q)
+        for (int s = 0; s < m; ++s)
+            for (int c = 0; c < KSUB4; ++c)
+                lut[(q * m + s) * KSUB4 + c] =
+                    l2sq(queries + q * d + (int64_t)s * dsub, centroids + ((int64_t)s * KSUB4 + c) * dsub, dsub);
+}
+
+void vko_adc_search_pq4(const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
+                        const float* queries, int64_t nq, int k, float* out_d, int32_t* out_i, int threads) {
+#ifdef _OPENMP
+    const int nt = threads > 0 ? threads : omp_get_max_threads();
+#else
+    const int nt = 1;
+    (void)threads;
+#endif
+    const int64_t d = (int64_t)m * dsub, mb = (m + 1) / 2;
+#pragma omp parallel num_threads(nt)
+    {
+        float* lut = (float*)malloc(sizeof(float) * (size_t)m * KSUB4);
+        float* hd = (float*)malloc(sizeof(float) * (size_t)(k > 0 ? k : 1));
+        int32_t* hi = (int32_t*)malloc(sizeof(int32_t) * (size_t)(k > 0 ? k : 1));
+#pragma omp for schedule(dynamic)
+        for (int64_t q = 0; q < nq; ++q) {
+            vko_compute_lut_pq4(centroids, m, dsub, queries + q * d, 1, lut);
+            topk_t t;
+            topk_init(&t, k, hd, hi);
+            for (int64_t i = 0; i < n; ++i) {
+                const uint8_t* row = codes + i * mb;
+                float acc = 0.f;
+                for (int s = 0; s < m; ++s) acc = acc + lut[s * KSUB4 + nib(row, s)];
+                topk_push(&t, acc, (int32_t)i);
+            }
+            topk_write(&t, out_d + q * k, out_i + q * k);
+        }
+        free(lut);
+        free(hd);
+        free(hi);
+    }
+}
+
 void vko_topk_push_all(const float* dists, const int32_t* ids, int64_t count, int k, float* out_d,
                        int32_t* out_i) {
     float* hd = (float*)malloc(sizeof(float) * (size_t)(k > 0 ? k : 1));

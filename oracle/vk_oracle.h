@@ -55,8 +55,6 @@ void vko_rerank_exact(const float* base, int d, const float* queries, int64_t nq
 double vko_recall_at_k(const int32_t* found, int64_t found_stride, const int32_t* truth, int64_t truth_stride,
                        int64_t nq, int k);
 
-/* Streaming search over codes that arrive in blocks (large configs: the codes never exist on the host at
- * once). Per query one bounded top-k; feed() must be called with ascending, non-overlapping id ranges. */
 /* Half-precision LUT search (the library's VK_LUT_F16 definition; see vk_oracle.c): the scaled, half-rounded
  * tables (as floats) with their per-query exponents, and the search over them. */
 void vko_compute_lut_h16(const float* centroids, int m, int dsub, const float* queries, int64_t nq, float* lut,
@@ -70,6 +68,15 @@ void vko_ivf_search(const float* centroids, int m, int dsub, const uint8_t* code
                     const float* coarse, int nlist, const float* queries, int64_t nq, int nprobe, int k,
                     float* out_d, int32_t* out_i, int32_t* probes_out, int threads);
 
+/* 4-bit PQ (the library's vk_index_create_pq4 definition; see vk_oracle.c): centroids [m][16][dsub], codes
+ * n x ceil(m / 2) bytes with sub-code s in nibble s % 2 (low first) of byte s / 2; lut: nq x m x 16. */
+void vko_pq4_encode(const float* centroids, int m, int dsub, const float* x, int64_t n, uint8_t* codes);
+void vko_compute_lut_pq4(const float* centroids, int m, int dsub, const float* queries, int64_t nq, float* lut);
+void vko_adc_search_pq4(const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
+                        const float* queries, int64_t nq, int k, float* out_d, int32_t* out_i, int threads);
+
+/* Streaming search over codes that arrive in blocks (large configs: the codes never exist on the host at
+ * once). Per query one bounded top-k; feed() must be called with ascending, non-overlapping id ranges. */
 typedef struct vko_stream vko_stream;
 vko_stream* vko_stream_create(const float* lut, int64_t nq, int m, int k);
 void vko_stream_feed(vko_stream* s, const uint8_t* codes, int64_t count, int64_t id_base, int threads);

@@ -128,3 +128,38 @@ def test_generated_codes_follow_their_cluster_distributions():
     freq = np.bincount(codes[:, 0], minlength=256) / codes.shape[0]
     assert np.abs(freq - w).max() < 0.01
     assert np.sort(w)[::-1][:26].sum() > 0.5  # top 10% of codes carry most of the mass
+
+
+def test_pq4_trainer_and_encoder():
+    """4-bit trainer: with no Lloyd iteration its 16 centroids per sub-space are the first 16 rows the reference's
+    draws pick (the 8-bit trainer, pinned to the reference, picks 256 with the same shuffles); one iteration replaces
+    each non-empty cluster's centroid by the float32 mean of its rows, summed in row order. The encoder equals the
+    oracle's restatement."""
+    import oracle
+
+    x = data.gen_mixture(0, 0, 400, 32, ncomp=20)
+    c8 = data.pq_train(x, 8, 0, 5)
+    c4 = data.pq4_train(x, 8, 0, 5)
+    assert c4.shape == (8, 16, 4) and np.array_equal(bits(c4), bits(c8[:, :16]))
+    c41 = data.pq4_train(x, 8, 1, 5)
+    for s in range(8):
+        xs = x[:, s * 4:(s + 1) * 4]
+        dist = np.zeros((400, 16), np.float32)
+        for c in range(16):
+            acc = np.zeros(400, np.float32)
+            for j in range(4):
+                diff = xs[:, j] - c4[s, c, j]
+                acc = acc + diff * diff
+            dist[:, c] = acc
+        assign = np.argmin(dist, 1)
+        for c in range(16):
+            rows = np.nonzero(assign == c)[0]
+            if rows.size == 0:
+                continue  # reseeded from an rng draw
+            acc = np.zeros(4, np.float32)
+            for r in rows:
+                acc = acc + xs[r]
+            assert np.array_equal(bits(c41[s, c]), bits(acc / np.float32(rows.size)))
+    codes = data.pq4_encode(c41, x)
+    assert codes.shape == (400, 4)
+    assert np.array_equal(codes, oracle.port().pq4_encode(c41, x))

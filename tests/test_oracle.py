@@ -183,3 +183,41 @@ def test_h16_definition_restated_in_numpy(port):
         dist = (acc.astype(np.float64) * 2.0 ** -int(exps[j])).astype(np.float32)
         order = np.lexsort((np.arange(n), dist))[:k]
         assert np.array_equal(i[j], order) and np.array_equal(bits(d[j]), bits(dist[order]))
+
+
+def _l2sq_rows(x, c):
+    """The reference's l2sq (common.hpp:27-34) for every row of x against one vector c, float32, j in order."""
+    acc = np.zeros(x.shape[0], np.float32)
+    for j in range(x.shape[1]):
+        diff = x[:, j] - c[j]
+        acc = acc + diff * diff
+    return acc
+
+
+def test_pq4_definition_restated_in_numpy(port):
+    """The oracle's 4-bit PQ (encode, LUT, search) against an independent numpy statement of the definition."""
+    rng = np.random.default_rng(12)
+    m, dsub, n, nq, k = 32, 4, 2_000, 6, 10
+    cent = rng.normal(size=(m, 16, dsub)).astype(np.float32)
+    x = rng.normal(size=(n, m * dsub)).astype(np.float32)
+    q = rng.normal(size=(nq, m * dsub)).astype(np.float32)
+    codes = port.pq4_encode(cent, x)
+    assert codes.shape == (n, m // 2)
+    sub = np.zeros((n, m), np.uint8)
+    for s in range(m):
+        dist = np.stack([_l2sq_rows(x[:, s * dsub:(s + 1) * dsub], cent[s, c]) for c in range(16)], 1)
+        sub[:, s] = np.argmin(dist, 1)  # first minimum
+    assert np.array_equal(codes, (sub[:, 0::2] | (sub[:, 1::2] << 4)).astype(np.uint8))
+    lut = port.compute_lut_pq4(cent, q)
+    for j in range(nq):
+        for s in range(m):
+            ref = np.array([_l2sq_rows(q[j:j + 1, s * dsub:(s + 1) * dsub], cent[s, c])[0] for c in range(16)],
+                           np.float32)
+            assert np.array_equal(bits(lut[j, s]), bits(ref))
+    d, i = port.adc_search_pq4(cent, codes, q, k)
+    for j in range(nq):
+        acc = np.zeros(n, np.float32)
+        for s in range(m):
+            acc = acc + lut[j, s, sub[:, s]]
+        order = np.lexsort((np.arange(n), acc))[:k]
+        assert np.array_equal(i[j], order) and np.array_equal(bits(d[j]), bits(acc[order]))

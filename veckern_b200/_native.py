@@ -66,6 +66,8 @@ ABI = {
     "vk_tuning_default": (None, [C.POINTER(Tuning)]),
     "vk_tuning_validate": (C.c_int, [C.POINTER(Tuning)]),
     "vk_index_create": (C.c_int, [C.c_int, _vp, C.c_int, C.c_int, _vp, _i64, _i64, C.POINTER(_vp)]),
+    "vk_index_create_pq4": (C.c_int, [C.c_int, _vp, C.c_int, C.c_int, _vp, _i64, _i64, C.POINTER(_vp)]),
+    "vk_index_bits": (C.c_int, [_vp, C.POINTER(C.c_int)]),
     "vk_index_create_from_device": (C.c_int, [C.c_int, _vp, C.c_int, C.c_int, _vp, _i64, _i64, C.POINTER(_vp)]),
     "vk_index_create_generated": (C.c_int, [C.c_int, _vp, C.c_int, C.c_int, _u64, _vp, C.c_int, _i64, _i64, _i64,
                                             C.POINTER(_vp)]),
@@ -114,6 +116,8 @@ HOST_ABI = {
     "vk_host_pq_train": (C.c_int, [_vp, _i64, C.c_int, C.c_int, _i64, _u64, _vp]),
     "vk_host_pq_encode": (C.c_int, [_vp, C.c_int, C.c_int, _vp, _i64, _vp]),
     "vk_host_pq_decode": (C.c_int, [_vp, C.c_int, C.c_int, _vp, _i64, _vp]),
+    "vk_host_pq4_train": (C.c_int, [_vp, _i64, C.c_int, C.c_int, _i64, _u64, _vp]),
+    "vk_host_pq4_encode": (C.c_int, [_vp, C.c_int, C.c_int, _vp, _i64, _vp]),
     "vk_host_synthetic_clustered": (C.c_int, [_i64, C.c_int, _i64, _u64, _vp]),
     "vk_host_gen_normal": (C.c_int, [_u64, _i64, _i64, C.c_int, _vp]),
     "vk_host_gen_mixture": (C.c_int, [_u64, C.c_int, C.c_float, _u64, _i64, _i64, C.c_int, _vp]),

@@ -62,6 +62,17 @@ def spec(name: str, **overrides) -> dict:
     return s
 
 
+def make_pq4(name: str, *, m: int = 32, n: int | None = None, nq: int | None = None, k: int | None = None,
+             keep_base: bool = False, rows: tuple[int, int] | None = None) -> Workload:
+    """4-bit PQ variant of a trained configuration (c0, c1, c2): the same database rows, queries and training sample,
+    with 16 centroids per sub-space trained by the same steps (data.pq4_train) and codes packed two per byte
+    (data.pq4_encode). m = 32 keeps config 1's 16 code bytes per row."""
+    w = make(name, n=n, m=m, nq=nq, k=k, keep_base=keep_base, rows=rows, train=data.pq4_train,
+             encode=data.pq4_encode)
+    w.extra["nbits"] = 4
+    return w
+
+
 def make(name: str, *, n: int | None = None, m: int | None = None, nq: int | None = None, k: int | None = None,
          keep_base: bool = False, encode=None, train=None, rows: tuple[int, int] | None = None) -> Workload:
     """Generates config `name` (optionally resized). encode(centroids, x) -> codes and train(x, m, iters, seed) ->
@@ -93,10 +104,13 @@ def make(name: str, *, n: int | None = None, m: int | None = None, nq: int | Non
             codes = enc(cent, x)
         else:  # large databases: generate and encode slice by slice, keeping only the codes
             x = None
-            codes = np.empty((hi - lo, s["m"]), np.uint8)
+            codes = None
             for a in range(lo, hi, SLICE_ROWS):
                 b = min(hi, a + SLICE_ROWS)
-                codes[a - lo:b - lo] = enc(cent, data.gen_mixture(s["mix_seed"], s["mix_seed"], b - a, d, row0=a))
+                part = enc(cent, data.gen_mixture(s["mix_seed"], s["mix_seed"], b - a, d, row0=a))
+                if codes is None:  # code bytes per row: m, or m / 2 for 4-bit codes
+                    codes = np.empty((hi - lo, part.shape[1]), np.uint8)
+                codes[a - lo:b - lo] = part
         w = Workload(name, s, cent, q, codes=codes, base=x if keep_base else None)
         w.extra["row0"] = lo
         return w

@@ -57,6 +57,12 @@ __global__ void interleave_kernel(const uint8_t* __restrict__ rows, int64_t row0
     }
 }
 
+// Identity lane placement (4-bit indexes): position p holds row p.
+__global__ void identity_perm_kernel(uint8_t* __restrict__ perm, int64_t n_pad) {
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < n_pad; p += (int64_t)gridDim.x * blockDim.x)
+        perm[p] = (uint8_t)(p & (PLACE_WINDOW - 1));
+}
+
 // Inverse of interleave_kernel + place_rows_kernel for rows [first, first + count): row-major output (tests and
 // tools). One thread per (position, sub-space) of the placement windows covering the rows.
 __global__ void deinterleave_kernel(const uint4* __restrict__ codes, const uint8_t* __restrict__ perm, int64_t first,

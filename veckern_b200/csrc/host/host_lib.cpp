@@ -35,11 +35,11 @@ inline float l2(const float* a, const float* b, int d) {
     return acc;
 }
 
-// First centroid with the strictly smallest distance (src/cpu/pq.cpp:11-22).
-inline int nearest(const float* x, const float* cents, int dsub) {
+// First centroid (of ksub) with the strictly smallest distance (src/cpu/pq.cpp:11-22).
+inline int nearest(const float* x, const float* cents, int dsub, int ksub = (int)kSubCentroids) {
     int best = 0;
     float best_d = FLT_MAX;
-    for (int c = 0; c < (int)kSubCentroids; ++c) {
+    for (int c = 0; c < ksub; ++c) {
         const float dist = l2(x, cents + (size_t)c * dsub, dsub);
         if (dist < best_d) {
             best_d = dist;
@@ -49,21 +49,25 @@ inline int nearest(const float* x, const float* cents, int dsub) {
     return best;
 }
 
-void train_impl(const float* x, size_t n, size_t d, size_t m, size_t iters, uint64_t seed, float* centroids) {
+// ksub = 256: the reference's trainer step for step. ksub = 16 (4-bit PQ, no counterpart in the reference): the same
+// steps with 16 centroids per sub-space.
+void train_impl(const float* x, size_t n, size_t d, size_t m, size_t iters, uint64_t seed, float* centroids,
+                size_t ksub = kSubCentroids) {
     const size_t dsub = d / m;
     std::mt19937_64 rng(seed);
-    std::vector<float> sub(n * dsub), sums(kSubCentroids * dsub);
-    std::vector<size_t> perm(n), assign(n), counts(kSubCentroids);
+    std::vector<float> sub(n * dsub), sums(ksub * dsub);
+    std::vector<size_t> perm(n), assign(n), counts(ksub);
     for (size_t s = 0; s < m; ++s) {
         for (size_t i = 0; i < n; ++i) std::memcpy(&sub[i * dsub], x + i * d + s * dsub, dsub * sizeof(float));
-        float* cent = centroids + s * kSubCentroids * dsub;
+        float* cent = centroids + s * ksub * dsub;
         std::iota(perm.begin(), perm.end(), size_t(0));
         std::shuffle(perm.begin(), perm.end(), rng);
-        for (size_t c = 0; c < kSubCentroids; ++c)
+        for (size_t c = 0; c < ksub; ++c)
             std::memcpy(cent + c * dsub, &sub[perm[c] * dsub], dsub * sizeof(float));
         for (size_t it = 0; it < iters; ++it) {
 #pragma omp parallel for schedule(static)
-            for (long long i = 0; i < (long long)n; ++i) assign[i] = (size_t)nearest(&sub[i * dsub], cent, (int)dsub);
+            for (long long i = 0; i < (long long)n; ++i)
+                assign[i] = (size_t)nearest(&sub[i * dsub], cent, (int)dsub, (int)ksub);
             std::fill(sums.begin(), sums.end(), 0.f);
             std::fill(counts.begin(), counts.end(), size_t(0));
             for (size_t i = 0; i < n; ++i) {
@@ -71,7 +75,7 @@ void train_impl(const float* x, size_t n, size_t d, size_t m, size_t iters, uint
                 ++counts[a];
                 for (size_t j = 0; j < dsub; ++j) sums[a * dsub + j] += sub[i * dsub + j];
             }
-            for (size_t c = 0; c < kSubCentroids; ++c) {
+            for (size_t c = 0; c < ksub; ++c) {
                 if (counts[c] == 0) {  // an empty cluster takes a random training row
                     std::memcpy(cent + c * dsub, &sub[(rng() % n) * dsub], dsub * sizeof(float));
                     continue;
@@ -89,6 +93,20 @@ void encode_impl(const float* centroids, size_t d, size_t m, const float* x, siz
         for (size_t s = 0; s < m; ++s)
             codes[(size_t)i * m + s] =
                 (uint8_t)nearest(x + (size_t)i * d + s * dsub, centroids + s * kSubCentroids * dsub, (int)dsub);
+}
+
+// 4-bit codes: nearest of 16 centroids per sub-space, sub-code s in nibble s % 2 (low first) of byte s / 2.
+void encode4_impl(const float* centroids, size_t d, size_t m, const float* x, size_t n, uint8_t* codes) {
+    const size_t dsub = d / m, mb = (m + 1) / 2;
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)n; ++i) {
+        uint8_t* row = codes + (size_t)i * mb;
+        std::memset(row, 0, mb);
+        for (size_t s = 0; s < m; ++s) {
+            const int c = nearest(x + (size_t)i * d + s * dsub, centroids + s * 16 * dsub, (int)dsub, 16);
+            row[s / 2] |= (uint8_t)(c << (4 * (s % 2)));
+        }
+    }
 }
 
 void decode_impl(const float* centroids, size_t d, size_t m, const uint8_t* codes, size_t n, float* x) {
@@ -178,6 +196,18 @@ int vk_host_pq_train(const float* x, int64_t n, int d, int m, int64_t iters, uin
 int vk_host_pq_encode(const float* centroids, int d, int m, const float* x, int64_t n, uint8_t* codes) {
     if (!centroids || !x || !codes || m <= 0 || d <= 0 || d % m != 0 || n < 0) return -1;
     encode_impl(centroids, (size_t)d, (size_t)m, x, (size_t)n, codes);
+    return 0;
+}
+
+int vk_host_pq4_train(const float* x, int64_t n, int d, int m, int64_t iters, uint64_t seed, float* centroids) {
+    if (!x || !centroids || m <= 0 || d <= 0 || d % m != 0 || n < 16 || iters < 0) return -1;
+    train_impl(x, (size_t)n, (size_t)d, (size_t)m, (size_t)iters, seed, centroids, 16);
+    return 0;
+}
+
+int vk_host_pq4_encode(const float* centroids, int d, int m, const float* x, int64_t n, uint8_t* codes) {
+    if (!centroids || !x || !codes || m <= 0 || d <= 0 || d % m != 0 || n < 0) return -1;
+    encode4_impl(centroids, (size_t)d, (size_t)m, x, (size_t)n, codes);
     return 0;
 }
 

@@ -9,6 +9,11 @@
 //              Q = 1: [s][c]; Q = 2: [s][c][2]; Q = 4: [s][c][4]; Q = 8: two [s][c][4] tables (queries 0-3, 4-7).
 //              One code byte then fetches all Q queries' entries with one LDS.32/64/128 (two LDS.128 for Q = 8).
 //              Half-precision LUTs (Q = 4 or 8): [s][c][Q] halves, one LDS.64 / LDS.128 per code byte.
+//              4-bit PQ (16 centroids per sub-space, Q = 4 or 8): [s][q / 2][c] float2 pairs: one sub-space table
+//              of two queries is 16 entries x 8 bytes = 128 bytes, one per bank pair, so a warp's LDS.64 into it
+//              never conflicts (2 wavefronts for 32 rows x 2 queries).
+//   4-bit codes sub-code s of a row in nibble s % 2 (low first) of byte s / 2; the bytes interleaved in 16-byte
+//              words as above (32 sub-codes per word).
 //   partials   [query][chunk][k] (dist, id) lists, merged by merge_kernel.
 #pragma once
 #include <cfloat>
@@ -112,6 +117,60 @@ __global__ void __launch_bounds__(256) ivf_lut_kernel(const float* __restrict__ 
         static_assert(Q == 8, "IVF items hold 4 or 8 queries");
         reinterpret_cast<float4*>(out)[e] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         reinterpret_cast<float4*>(out)[m * KSUB + e] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+}
+
+// ---- 4-bit PQ: 16 centroids per sub-space, centroids [m][16][dsub]
+constexpr int KSUB4 = 16;
+
+// grid (ceil(m / 16), groups), block 256: thread t computes centroid t % 16 of sub-space 16 * blockIdx.x + t / 16
+// for the Q queries of group g, with the arithmetic of lut_entries, and writes the scan layout [s][q / 2][c] of
+// float2 pairs. Blocks with blockIdx.x == 0 reset the pruned scan's per-query state (bound, global list, lock).
+template <int Q>
+__global__ void __launch_bounds__(256) lut4_kernel(const float* __restrict__ centroids,
+                                                   const float* __restrict__ queries, int64_t nq, int m, int dsub,
+                                                   float* __restrict__ lut, uint32_t* __restrict__ bound,
+                                                   int2* __restrict__ glist, int* __restrict__ glock, int k) {
+    static_assert(Q % 2 == 0, "4-bit LUT entries hold query pairs");
+    extern __shared__ float qsub4[];  // [Q][16][dsub]: the group's query sub-vectors of the block's 16 sub-spaces
+    const int s0 = blockIdx.x * 16, g = blockIdx.y;
+    const int ns = min(16, m - s0);
+    const int64_t d = (int64_t)m * dsub;
+    for (int t = threadIdx.x; t < Q * ns * dsub; t += blockDim.x) {
+        const int qq = t / (ns * dsub), r = t - qq * ns * dsub;
+        const int64_t qi = (int64_t)g * Q + qq;
+        qsub4[qq * 16 * dsub + r] = qi < nq ? queries[qi * d + (int64_t)s0 * dsub + r] : 0.f;
+    }
+    if (bound && blockIdx.x == 0) {
+        for (int t = threadIdx.x; t < Q * k; t += blockDim.x) {
+            const int64_t qi = (int64_t)g * Q + t / k;
+            if (qi < nq) glist[qi * k + t % k] = make_int2(0x7f800000, SENTINEL_ID);
+        }
+        if (threadIdx.x < Q && (int64_t)g * Q + threadIdx.x < nq) {
+            bound[(int64_t)g * Q + threadIdx.x] = 0x7f800000u;
+            glock[(int64_t)g * Q + threadIdx.x] = 0;
+        }
+    }
+    __syncthreads();
+    const int sl = threadIdx.x >> 4, c = threadIdx.x & 15, s = s0 + sl;
+    if (sl >= ns) return;
+    const float* cen = centroids + ((int64_t)s * KSUB4 + c) * dsub;
+    float acc[Q];
+#pragma unroll
+    for (int qq = 0; qq < Q; ++qq) acc[qq] = 0.f;
+    for (int j = 0; j < dsub; ++j) {
+        const float cj = cen[j];
+#pragma unroll
+        for (int qq = 0; qq < Q; ++qq) {
+            const float diff = __fsub_rn(qsub4[(qq * 16 + sl) * dsub + j], cj);
+            acc[qq] = __fadd_rn(acc[qq], __fmul_rn(diff, diff));
+        }
+    }
+    float2* out = reinterpret_cast<float2*>(lut + (int64_t)g * Q * m * KSUB4);
+#pragma unroll
+    for (int qp = 0; qp < Q / 2; ++qp) {
+        const bool v0 = (int64_t)g * Q + 2 * qp < nq, v1 = (int64_t)g * Q + 2 * qp + 1 < nq;
+        out[((int64_t)s * (Q / 2) + qp) * KSUB4 + c] = make_float2(v0 ? acc[2 * qp] : 0.f, v1 ? acc[2 * qp + 1] : 0.f);
     }
 }
 
@@ -225,15 +284,22 @@ struct ScanArgs {
     int nprobe;
 };
 
-// Bound of query qi from the other shards of a cooperative search (+inf bits when there is none yet).
-__device__ __forceinline__ uint32_t coop_bound(const ScanArgs& a, int64_t qi) {
-    if (!a.xb) return 0x7f800000u;
-    const unsigned long long v = __ldcg(a.xb + qi);
-    return (uint32_t)(v >> 32) == a.epoch ? 0xffffffffu - (uint32_t)v : 0x7f800000u;
+// Bound of query qi from the other shards of a cooperative search (+inf bits when there is none yet), in two steps
+// so that a caller can issue the load early and combine it later: coop_load reads the exchange entry (0 without an
+// exchange), coop_decode turns it into float bits.
+__device__ __forceinline__ unsigned long long coop_load(const ScanArgs& a, int64_t qi) {
+    return a.xb ? __ldcg(a.xb + qi) : 0ull;
 }
-// Offers a lowered bound of query qi to the other shards (posted system-scope atomics over NVLink).
+__device__ __forceinline__ uint32_t coop_decode(const ScanArgs& a, unsigned long long v) {
+    return a.xb && (uint32_t)(v >> 32) == a.epoch ? 0xffffffffu - (uint32_t)v : 0x7f800000u;
+}
+__device__ __forceinline__ uint32_t coop_bound(const ScanArgs& a, int64_t qi) { return coop_decode(a, coop_load(a, qi)); }
+// Offers a lowered bound of query qi to the other shards (posted system-scope atomics over NVLink). The loop stays
+// rolled: unrolled at every publishing site it made the scan kernel's code a fifth larger (instruction-cache misses
+// in the per-tile loop).
 __device__ __forceinline__ void coop_publish(const ScanArgs& a, int64_t qi, uint32_t bits) {
     const unsigned long long v = ((unsigned long long)a.epoch << 32) | (unsigned long long)(0xffffffffu - bits);
+#pragma unroll 1
     for (int p = 0; p < a.npeers; ++p) atomicMax_system(a.xpeer[p] + qi, v);
 }
 
@@ -255,11 +321,13 @@ __host__ __device__ constexpr bool carry_queue(int m) { return m == 16; }
 // and the phase-A depth, 2 bits).
 constexpr int64_t CARRY_MAX_CHUNK_ROWS = int64_t(1) << 23;
 
+// p4: 4-bit PQ (16-entry sub-space tables, W words of 32 sub-codes per row, no carry queue).
 __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp, int nw, int stages, int k,
-                                                   bool prune, int merge_slots, bool h16, bool ivf = false) {
+                                                   bool prune, int merge_slots, bool h16, bool ivf = false,
+                                                   bool p4 = false) {
     auto up = [](uint32_t x, uint32_t a) { return (x + a - 1) / a * a; };
     ScanSmem p;
-    p.lut_bytes = (uint32_t)Q * m * KSUB * (h16 ? 2u : 4u);
+    p.lut_bytes = (uint32_t)Q * m * (p4 ? KSUB4 : KSUB) * (h16 ? 2u : 4u);
     p.tile_bytes = (uint32_t)ilp * W * 512u;
     // codes, then the tile's placement bytes, then (IVF) the ids of the tile's 64-row window
     p.stage_bytes = p.tile_bytes + (uint32_t)ilp * 32u + (ivf ? 256u : 0u);
@@ -269,8 +337,8 @@ __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp,
     p.queue = up(p.scratch + (uint32_t)merge_slots * nw * k * 8u, 16);
     // m = 16: the carry queue (CARRY_CAP 16-byte entries per warp); other m: at most half a tile's (row, query)
     // pairs, 8 bytes each (with more survivors the tile is finished in full)
-    const uint32_t queue_bytes = !prune ? 0u : carry_queue(m) ? (uint32_t)nw * CARRY_CAP * 16u
-                                                              : (uint32_t)nw * 16u * ilp * Q * 8u;
+    const uint32_t queue_bytes = !prune ? 0u : carry_queue(m) && !p4 ? (uint32_t)nw * CARRY_CAP * 16u
+                                                                     : (uint32_t)nw * 16u * ilp * Q * 8u;
     p.ring = up(p.queue + queue_bytes, 16);
     p.bars = up(p.ring + (uint32_t)nw * stages * 4u, 16);
     p.flags = p.bars + (uint32_t)(nw * stages + 1) * 8u;
@@ -290,8 +358,13 @@ __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp,
 // its window; ids, and so results, are those of the rows.
 constexpr int PLACE_WINDOW = 64;
 
-__host__ __device__ constexpr int prune_first(int m) { return m <= 16 ? 8 : m <= 32 ? 12 : 24; }
-__host__ __device__ constexpr int prune_last(int m) { return m <= 16 ? 12 : m <= 32 ? 16 : 28; }
+// 4-bit codes (p4) carry half the bits per sub-space: their first vote comes after half of the sub-spaces.
+__host__ __device__ constexpr int prune_first(int m, bool p4 = false) {
+    return p4 ? m / 2 : m <= 16 ? 8 : m <= 32 ? 12 : 24;
+}
+__host__ __device__ constexpr int prune_last(int m, bool p4 = false) {
+    return p4 ? m / 2 + (m <= 16 ? 4 : 8) : m <= 16 ? 12 : m <= 32 ? 16 : 28;
+}
 constexpr int PRUNE_DEEPEN = 8;
 
 // Adds the 2 halves of a 32-bit word to acc[0], acc[1]: the mixed-precision add of sm_100 (add.rn.f32.f16)
@@ -351,15 +424,24 @@ __device__ __forceinline__ void lookup_add(const unsigned char* lut_smem, int mt
     }
 }
 
-// Byte offset of query q's entry (s = 0, c = 0) in the group's LUT, and the stride between c entries.
-template <int Q, bool H16>
+// Byte offset of query q's entry (s = 0, c = 0) in the group's LUT, the stride between c entries, and the offset of
+// entry (s, c) from the query's base (P4: 4-bit PQ's [s][q / 2][c] float2 tables).
+template <int Q, bool H16, bool P4 = false>
 __device__ __forceinline__ uint32_t lut_query_base(int q, int mtab) {
-    if constexpr (H16) return (uint32_t)q * 2u;
+    if constexpr (P4) return (uint32_t)(q >> 1) * 128u + (uint32_t)(q & 1) * 4u;
+    else if constexpr (H16) return (uint32_t)q * 2u;
     else if constexpr (Q >= 4) return (uint32_t)(q >> 2) * (uint32_t)mtab * KSUB * 16u + (uint32_t)(q & 3) * 4u;
     else return (uint32_t)q * 4u;
 }
-template <int Q, bool H16>
-__host__ __device__ constexpr uint32_t lut_entry_bytes() { return H16 ? (uint32_t)Q * 2u : Q >= 4 ? 16u : (uint32_t)Q * 4u; }
+template <int Q, bool H16, bool P4 = false>
+__host__ __device__ constexpr uint32_t lut_entry_bytes() {
+    return P4 ? 8u : H16 ? (uint32_t)Q * 2u : Q >= 4 ? 16u : (uint32_t)Q * 4u;
+}
+template <int Q, bool H16, bool P4 = false>
+__device__ __forceinline__ uint32_t lut_pos(int s, uint32_t c) {
+    if constexpr (P4) return (uint32_t)s * (uint32_t)(Q * 64) + c * 8u;
+    else return ((uint32_t)s * KSUB + c) * lut_entry_bytes<Q, H16>();
+}
 // One query's entry at byte address p of the shared LUT, as fp32.
 template <bool H16>
 __device__ __forceinline__ float lut_value(const unsigned char* p) {
@@ -372,6 +454,27 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int b) {
 }
 
 __device__ __forceinline__ uint32_t code_byte(const uint4& v, int b) { return (word_of(v, b) >> (8 * (b & 3))) & 0xffu; }
+
+// 4-bit codes: sub-code j (0..31) of a 16-byte word, and 8 times it (the byte offset of its float2 LUT entry).
+__device__ __forceinline__ uint32_t code_nib(const uint4& v, int j) { return (word_of(v, j >> 1) >> (4 * (j & 7))) & 0xfu; }
+__device__ __forceinline__ uint32_t code_nib8(const uint4& v, int j) {
+    const uint32_t w = word_of(v, j >> 1);
+    const int sh = 4 * (j & 7);
+    return sh >= 3 ? (w >> (sh - 3)) & 0x78u : (w << 3) & 0x78u;
+}
+
+// 4-bit PQ: one sub-space lookup for Q queries, Q / 2 conflict-free LDS.64 from the [s][q / 2][c] float2 tables
+// (c8 = 8 * code); acc[q] += LUT_q[s][c], rounded per add, in s order.
+template <int Q>
+__device__ __forceinline__ void lookup_add4(const unsigned char* lut_smem, int s, uint32_t c8, float* acc) {
+    const unsigned char* p = lut_smem + (uint32_t)s * (uint32_t)(Q * 64) + c8;
+#pragma unroll
+    for (int qp = 0; qp < Q / 2; ++qp) {
+        const float2 v = *reinterpret_cast<const float2*>(p + qp * 128);
+        acc[2 * qp] = __fadd_rn(acc[2 * qp], v.x);
+        acc[2 * qp + 1] = __fadd_rn(acc[2 * qp + 1], v.y);
+    }
+}
 
 // Persistent fused scan + top-k. Work item = (vector chunk, query group), handed out by an atomic counter in
 // chunk-major order, so the blocks running at one time share the same chunk of codes through L2.
@@ -393,27 +496,32 @@ __device__ __forceinline__ uint32_t code_byte(const uint4& v, int b) { return (w
 // for one block, which then has 16 warps. Either way 16 warps per SM, registers capped at 128.
 // Half-precision LUTs always take 16-warp blocks: two 8-warp blocks with their own 64 KB LUTs, rings and queues do
 // not fit one SM's shared memory together, which left one 8-warp block per SM (measured: 12.5 % warps active).
-__host__ __device__ constexpr int scan_warps(int Q, int MT, bool H16 = false) {
-    return !H16 && Q * (MT ? MT : 16) * KSUB * 4 <= 80 * 1024 ? 8 : 16;
+// 4-bit PQ LUTs (at most 8 queries x 64 sub-spaces x 16 entries x 4 bytes = 32 KB) always take two 8-warp blocks.
+__host__ __device__ constexpr int scan_warps(int Q, int MT, bool H16 = false, bool P4 = false) {
+    return P4 || (!H16 && Q * (MT ? MT : 16) * KSUB * 4 <= 80 * 1024) ? 8 : 16;
 }
-template <int Q, int MT, bool H16>
-constexpr int scan_min_blocks() { return scan_warps(Q, MT, H16) == 8 ? 2 : 1; }
+template <int Q, int MT, bool H16, bool P4>
+constexpr int scan_min_blocks() { return scan_warps(Q, MT, H16, P4) == 8 ? 2 : 1; }
 
 // H16: half-precision LUT entries (Q = 4 or 8, m = 16, 32 or 64), summed in fp32 like the fp32 entries.
 // IVF: items are (list, up to Q queries probing it) from the IVF item table; ids come from the index's id array.
-template <int Q, int MT, int ILP, int S, int NW, bool PRUNE, bool H16 = false, bool IVF = false>
-__global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_kernel(const ScanArgs a) {
+// P4: 4-bit PQ codes (16 centroids per sub-space, 32 sub-codes per 16-byte word) and their float2-pair LUTs.
+template <int Q, int MT, int ILP, int S, int NW, bool PRUNE, bool H16 = false, bool IVF = false, bool P4 = false>
+__global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16, P4>()) scan_kernel(const ScanArgs a) {
     static_assert(!IVF || (ILP <= 2 && !H16), "IVF items start on 64-row windows; fp32 LUTs");
     static_assert(!H16 || (MT != 0 && (Q == 4 || Q == 8)), "half LUTs: m = 16, 32, 64 and 4 or 8 queries");
+    static_assert(!P4 || (MT != 0 && (Q == 4 || Q == 8) && !H16 && !IVF), "4-bit PQ: m = 16, 32, 64, Q = 4 or 8");
     static_assert(!PRUNE || MT != 0, "the pruned scan is specialised for m = 16, 32, 64");
     extern __shared__ __align__(128) unsigned char smem[];
-    constexpr int W_T = MT ? (MT + 15) / 16 : 0;
-    constexpr int SA = prune_first(MT), SAX = prune_last(MT);
+    constexpr int SPW = P4 ? 32 : 16;  // sub-codes per 16-byte word
+    constexpr int W_T = MT ? (MT + SPW - 1) / SPW : 0;
+    constexpr int SA = prune_first(MT, P4), SAX = prune_last(MT, P4);
+    constexpr bool CARRY = carry_queue(MT) && !P4;
     static_assert(!PRUNE || (SA % 2 == 0 && SAX % 2 == 0 && SAX >= SA && SAX < MT),
                   "phase A stops at even sub-spaces: phase B fetches sub-spaces in pairs inside one 16-byte word");
     const int m = MT ? MT : a.m;
     const int W = MT ? W_T : a.W;
-    const ScanSmem plan = scan_smem_plan(Q, m, W, ILP, NW, a.stages, a.k, PRUNE, a.merge_slots, H16, IVF);
+    const ScanSmem plan = scan_smem_plan(Q, m, W, ILP, NW, a.stages, a.k, PRUNE, a.merge_slots, H16, IVF, P4);
     unsigned char* lut_smem = smem + plan.lut;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + plan.bars);
     uint64_t* lut_bar = bars + NW * a.stages;
@@ -528,7 +636,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_k
 #pragma unroll
             for (int qq = 1; qq < Q; ++qq)
                 if (q == qq) bq = fminf(known[qq], top[qq].thr_d);
-            const unsigned char* lq = lut_smem + lut_query_base<Q, H16>(q, MT);
+            const unsigned char* lq = lut_smem + lut_query_base<Q, H16, P4>(q, MT);
             bool live = in && !(x > bq);  // the bound may have dropped since the pair was queued
 #pragma unroll
             for (int t = 0; t < (MT - SA) / 2; ++t) {
@@ -538,8 +646,8 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_k
                     const uint32_t c0 = lo & 0xffu, c1 = (lo >> 8) & 0xffu;
                     lo = __funnelshift_r(lo, hi, 16);
                     hi >>= 16;
-                    const float v0 = lut_value<H16>(lq + ((uint32_t)s * KSUB + c0) * lut_entry_bytes<Q, H16>());
-                    const float v1 = lut_value<H16>(lq + ((uint32_t)(s + 1) * KSUB + c1) * lut_entry_bytes<Q, H16>());
+                    const float v0 = lut_value<H16>(lq + lut_pos<Q, H16, P4>(s, c0));
+                    const float v1 = lut_value<H16>(lq + lut_pos<Q, H16, P4>(s + 1, c1));
                     x = __fadd_rn(x, v0);
                     live = !(x > bq);
                     x = __fadd_rn(x, v1);
@@ -594,11 +702,20 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_k
                 refill();
                 if (issued == before) break;
             }
+        // fin: the chunk has no tiles left. The carry queue is drained at one place, the top of this loop: full
+        // batches after each tile, every entry once the tiles are done (one inlined copy of the batch code and its
+        // Q top-k offers instead of two keeps the kernel's instruction footprint down).
+        bool fin = false;
         while (!warp_abort) {
+            if constexpr (PRUNE && CARRY) carry_drain(fin);
+            if (fin) break;
             __syncwarp();  // ring entries written by lane 0 are visible
             const uint32_t slot = consumed % (uint32_t)a.stages;
             const int tile = my_ring[slot];
-            if (tile < 0 || consumed == __shfl_sync(FULL, issued, 0)) break;  // the chunk has no tiles left
+            if (tile < 0 || consumed == __shfl_sync(FULL, issued, 0)) {
+                fin = true;
+                continue;
+            }
             const uint32_t parity = (consumed / (uint32_t)a.stages) & 1u;
             if (!__all_sync(FULL, mbar_wait_bounded(my_bars + slot, parity, a.wait_budget))) {
                 if (lane == 0) atomicOr(a.status, ERR_WAIT_TIMEOUT);
@@ -640,16 +757,18 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_k
 #pragma unroll
                         for (int u = 0; u < ILP; ++u) cv[u] = st[(u * W + ww) * 32 + lane];
 #pragma unroll
-                        for (int b = 0; b < 16; ++b) {
-                            const int s = ww * 16 + b;
-                            if (!MT && s >= m) break;
+                        for (int b = 0; b < SPW; ++b) {
+                            const int s = ww * SPW + b;
+                            if ((!MT || P4) && s >= m) break;  // P4: MT = 16 fills half a word
 #pragma unroll
-                            for (int u = 0; u < ILP; ++u) lookup_add<Q, H16>(lut_smem, m, s, code_byte(cv[u], b), acc[u]);
+                            for (int u = 0; u < ILP; ++u) {
+                                if constexpr (P4) lookup_add4<Q>(lut_smem, s, code_nib8(cv[u], b), acc[u]);
+                                else lookup_add<Q, H16>(lut_smem, m, s, code_byte(cv[u], b), acc[u]);
+                            }
                         }
                     }
                 }
                 int32_t ids[ILP];
-#pragma unroll
                 bool valid[ILP];
 #pragma unroll
                 for (int u = 0; u < ILP; ++u) {  // both read the stage slot (IVF), so before it is refilled
@@ -666,18 +785,25 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_k
                     for (int q = 0; q < Q; ++q) any |= valid[u] && top[q].admits(acc[u][q], ids[u]);
                 }
                 if (__any_sync(FULL, any)) {
+                    static_for<Q>([&](auto qc) {
+                        constexpr int q = decltype(qc)::value;
+                        float x[ILP];
 #pragma unroll
-                    for (int u = 0; u < ILP; ++u)
-#pragma unroll
-                        for (int q = 0; q < Q; ++q) top[q].offer(acc[u][q], ids[u], valid[u], a.k);
+                        for (int u = 0; u < ILP; ++u) x[u] = acc[u][q];
+                        top[q].offer_n(x, ids, valid, a.k);
+                    });
                 }
             } else {
                 // The query group's global bounds, loaded now (lane q: query q) so that the L2 latency hides
                 // behind phase A; other warps and blocks keep lowering them.
-                float gb = __int_as_float(0x7f800000);
+                uint32_t gbits = 0x7f800000u;
+                unsigned long long gx = 0ull;
                 if (lane < Q) {
                     const int64_t qi = qidx(lane);
-                    if (qi >= 0) gb = __uint_as_float(min(__ldcg(a.bound + qi), coop_bound(a, qi)));
+                    if (qi >= 0) {
+                        gbits = __ldcg(a.bound + qi);
+                        gx = coop_load(a, qi);
+                    }
                 }
                 // ---- phase A: sub-spaces [0, SA) of every row, all Q queries per fetch
                 float acc[ILP][Q];
@@ -688,14 +814,18 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_k
                 uint4 cv[ILP];
                 auto phase_a = [&](auto sc) {  // one sub-space (a compile-time constant) of every row
                     constexpr int s = decltype(sc)::value;
-                    if constexpr (s % 16 == 0) {
+                    if constexpr (s % SPW == 0) {
 #pragma unroll
-                        for (int u = 0; u < ILP; ++u) cv[u] = st[(u * W_T + s / 16) * 32 + lane];
+                        for (int u = 0; u < ILP; ++u) cv[u] = st[(u * W_T + s / SPW) * 32 + lane];
                     }
 #pragma unroll
-                    for (int u = 0; u < ILP; ++u) lookup_add<Q, H16>(lut_smem, MT, s, code_byte(cv[u], s % 16), acc[u]);
+                    for (int u = 0; u < ILP; ++u) {
+                        if constexpr (P4) lookup_add4<Q>(lut_smem, s, code_nib8(cv[u], s % SPW), acc[u]);
+                        else lookup_add<Q, H16>(lut_smem, MT, s, code_byte(cv[u], s % 16), acc[u]);
+                    }
                 };
                 static_for<SA>(phase_a);
+                const float gb = __uint_as_float(min(gbits, coop_decode(a, gx)));  // the loads have landed by now
                 float bnd[Q];
 #pragma unroll
                 for (int q = 0; q < Q; ++q) {
@@ -740,13 +870,20 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_k
                         for (int q = 0; q < Q; ++q) any |= alive(u, q) && top[q].admits(acc[u][q], ids[u]);
                     }
                     if (__any_sync(FULL, any)) {
+                        static_for<Q>([&](auto qc) {
+                            constexpr int q = decltype(qc)::value;
+                            float x[ILP];
+                            bool v[ILP];
 #pragma unroll
-                        for (int u = 0; u < ILP; ++u)
-#pragma unroll
-                            for (int q = 0; q < Q; ++q) top[q].offer(acc[u][q], ids[u], alive(u, q), a.k);
+                            for (int u = 0; u < ILP; ++u) {
+                                x[u] = acc[u][q];
+                                v[u] = alive(u, q);
+                            }
+                            top[q].offer_n(x, ids, v, a.k);
+                        });
                     }
                 };
-                if constexpr (carry_queue(MT)) {
+                if constexpr (CARRY) {
                     static_assert(CARRY_QWIDE * PRUNE_DEEPEN >= 32 * ILP * Q,
                                   "a tile with more than CARRY_QWIDE survivors must have been deepened to SAX");
                     if (total > CARRY_QWIDE) {
@@ -780,16 +917,22 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_k
                             uint32_t* ent = reinterpret_cast<uint32_t*>(my_carry + e);
                             const uint32_t y = ent[1];
                             const uint32_t r = y & 0xffffu;
-                            const uint4 w = st[r];  // the row's 16 sub-codes
                             float x = __uint_as_float(ent[0]);
-                            if (dep < CARRY_DEPTH0) {  // warp-uniform
-                                const unsigned char* lq = lut_smem + lut_query_base<Q, H16>((int)(y >> 24), MT);
-                                for (int sb = dep; sb < CARRY_DEPTH0; ++sb)
-                                    x = __fadd_rn(x, lut_value<H16>(lq + ((uint32_t)sb * KSUB + code_byte(w, sb)) *
-                                                                             lut_entry_bytes<Q, H16>()));
+                            uint32_t lo, hi;
+                            if constexpr (SA < CARRY_DEPTH0) {
+                                const uint4 w = st[r];  // the row's 16 sub-codes
+                                if (dep < CARRY_DEPTH0) {  // warp-uniform
+                                    const unsigned char* lq = lut_smem + lut_query_base<Q, H16>((int)(y >> 24), MT);
+                                    for (int sb = dep; sb < CARRY_DEPTH0; ++sb)
+                                        x = __fadd_rn(x, lut_value<H16>(lq + lut_pos<Q, H16>(sb, code_byte(w, sb))));
+                                }
+                                lo = d0 == 8 ? w.z : d0 == 10 ? __funnelshift_r(w.z, w.w, 16) : w.w;
+                                hi = d0 == 8 ? w.w : d0 == 10 ? w.w >> 16 : 0u;
+                            } else {  // phase A never stops before CARRY_DEPTH0: only bytes 8..15 are needed
+                                const uint2 zw = reinterpret_cast<const uint2*>(st + r)[1];
+                                lo = d0 == 8 ? zw.x : d0 == 10 ? __funnelshift_r(zw.x, zw.y, 16) : zw.y;
+                                hi = d0 == 8 ? zw.y : d0 == 10 ? zw.y >> 16 : 0u;
                             }
-                            const uint32_t lo = d0 == 8 ? w.z : d0 == 10 ? __funnelshift_r(w.z, w.w, 16) : w.w;
-                            const uint32_t hi = d0 == 8 ? w.w : d0 == 10 ? w.w >> 16 : 0u;
                             const uint32_t rel = ((tile_rel + r) & ~(uint32_t)(PLACE_WINDOW - 1)) + st_perm[r];
                             reinterpret_cast<uint4*>(ent)[0] =
                                 make_uint4(__float_as_uint(x), rel | (y & (7u << 24)) | (dsel << 27), lo, hi);
@@ -797,7 +940,6 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_k
                     }
                     __syncwarp();  // the stage slot is free: queued pairs carry their codes
                     if (lane == 0) refill();
-                    carry_drain(false);
                 } else {
                 int cnt = 0;
                 if (2 * total > 32 * ILP * Q) {
@@ -836,21 +978,22 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_k
 #pragma unroll
                         for (int qq = 1; qq < Q; ++qq)
                             if (q == qq) bq = bnd[qq];
-                        const unsigned char* lq = lut_smem + lut_query_base<Q, H16>(q, MT);
+                        const unsigned char* lq = lut_smem + lut_query_base<Q, H16, P4>(q, MT);
                         const uint4* rowp = st + (r >> 5) * W_T * 32 + (r & 31);
                         uint4 cw = make_uint4(0, 0, 0, 0);
 #pragma unroll
                         for (int s = D; s < MT; s += 2) {
-                            if (s == D || s % 16 == 0) {
+                            if (s == D || s % SPW == 0) {
                                 if (!__any_sync(FULL, live)) break;
-                                if (live) cw = rowp[(s / 16) * 32];
+                                if (live) cw = rowp[(s / SPW) * 32];
                             } else if ((s - D) % 4 == 0 && !__any_sync(FULL, live)) {
                                 break;
                             }
                             if (live) {
-                                const uint32_t c0 = code_byte(cw, s % 16), c1 = code_byte(cw, (s + 1) % 16);
-                                const float v0 = lut_value<H16>(lq + ((uint32_t)s * KSUB + c0) * lut_entry_bytes<Q, H16>());
-                                const float v1 = lut_value<H16>(lq + ((uint32_t)(s + 1) * KSUB + c1) * lut_entry_bytes<Q, H16>());
+                                const uint32_t c0 = P4 ? code_nib(cw, s % SPW) : code_byte(cw, s % 16);
+                                const uint32_t c1 = P4 ? code_nib(cw, (s + 1) % SPW) : code_byte(cw, (s + 1) % 16);
+                                const float v0 = lut_value<H16>(lq + lut_pos<Q, H16, P4>(s, c0));
+                                const float v1 = lut_value<H16>(lq + lut_pos<Q, H16, P4>(s + 1, c1));
                                 x = __fadd_rn(x, v0);
                                 live = !(x > bq);
                                 x = __fadd_rn(x, v1);
@@ -892,10 +1035,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_k
                 }
             }
         }
-        if constexpr (PRUNE && carry_queue(MT)) {
-            if (!warp_abort) carry_drain(true);  // queued pairs of the item's last tiles
-            qcnt = 0;
-        }
+        if constexpr (PRUNE && CARRY) qcnt = 0;  // drained at the loop's end, or abandoned on a timeout
         if (warp_abort && lane == 0) {
             // Let this warp's copies still in flight land before the block can exit.
             while (consumed < issued) {
@@ -955,30 +1095,24 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16>()) scan_k
                 }
             }
         };
-        if (a.merge_slots >= Q) {
-#pragma unroll
-            for (int q = 0; q < Q; ++q) top[q].store(scratch + (q * NW + warp) * a.k, a.k);
+        // merge_slots queries at a time (Q, or 1 when Q lists per warp do not fit the scratch), query q0 + j merged
+        // by warp j: one call site for merge_and_publish (its code is large and runs once per item).
+        for (int q0 = 0; q0 < Q; q0 += a.merge_slots) {
+            static_for<Q>([&](auto qc) {
+                constexpr int q = decltype(qc)::value;
+                if (q >= q0 && q < q0 + a.merge_slots) top[q].store(scratch + ((q - q0) * NW + warp) * a.k, a.k);
+            });
             __syncthreads();
-            const int64_t qi = warp < Q ? qidx(warp) : -1;
+            const int ql = q0 + warp;
+            const int64_t qi = warp < a.merge_slots && ql < Q ? qidx(ql) : -1;
             float kb = __int_as_float(0x7f800000);
             if constexpr (PRUNE) {
-#pragma unroll
-                for (int q = 0; q < Q; ++q)
-                    if (warp == q) kb = known[q];
+                static_for<Q>([&](auto qc) {
+                    if (ql == decltype(qc)::value) kb = known[decltype(qc)::value];
+                });
             }
-            if (qi >= 0) merge_and_publish(qi, warp, scratch + warp * NW * a.k, kb);
+            if (qi >= 0) merge_and_publish(qi, ql, scratch + warp * NW * a.k, kb);
             __syncthreads();
-        } else {
-#pragma unroll
-            for (int q = 0; q < Q; ++q) {
-                const int64_t qi = qidx(q);
-                if (qi >= 0) {  // uniform
-                    top[q].store(scratch + warp * a.k, a.k);
-                    __syncthreads();
-                    if (warp == 0) merge_and_publish(qi, q, scratch, PRUNE ? known[q] : __int_as_float(0x7f800000));
-                    __syncthreads();
-                }
-            }
         }
     }
     // A LUT copy whose wait ran out may still be in flight: it must land before the block's shared memory is

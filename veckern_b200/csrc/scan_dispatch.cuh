@@ -15,6 +15,9 @@ const void* scan_kernel_h16_for(int mt, int ilp, int s, bool prune);
 // IVF items: Q in {4, 8}, mt in {16, 32}, ilp in {1, 2}, fp32 LUTs.
 template <int Q>
 const void* scan_kernel_ivf_for(int mt, int ilp, int s, bool prune);
+// 4-bit PQ: Q in {4, 8}, mt in {16, 32, 64}, ilp in {1, 2}, fp32 LUTs.
+template <int Q>
+const void* scan_kernel_p4_for(int mt, int ilp, int s, bool prune);
 
 #define VK_SCAN_CASE(Q, MT, ILP, S, P)            \
     case (P) * 10000 + MT * 100 + ILP * 10 + S: \
@@ -72,6 +75,25 @@ const void* scan_kernel_ivf_for(int mt, int ilp, int s, bool prune);
         switch ((prune ? 10000 : 0) + mt * 100 + ilp * 10 + s) {            \
             VK_SCAN_CASES_I_MT(Q, 16)                                       \
             VK_SCAN_CASES_I_MT(Q, 32)                                       \
+            default: return nullptr;                                        \
+        }                                                                   \
+    }
+
+#define VK_SCAN_CASE_P4(Q, MT, ILP, S, P)         \
+    case (P) * 10000 + MT * 100 + ILP * 10 + S: \
+        return reinterpret_cast<const void*>(&scan_kernel<Q, MT, ILP, S, scan_warps(Q, MT, false, true), P, false, false, true>);
+#define VK_SCAN_CASES_P4_S(Q, MT, ILP, P) VK_SCAN_CASE_P4(Q, MT, ILP, 1, P) VK_SCAN_CASE_P4(Q, MT, ILP, 2, P) VK_SCAN_CASE_P4(Q, MT, ILP, 4, P)
+#define VK_SCAN_CASES_P4_MT(Q, MT)                                                                            \
+    VK_SCAN_CASES_P4_S(Q, MT, 1, false) VK_SCAN_CASES_P4_S(Q, MT, 2, false) VK_SCAN_CASES_P4_S(Q, MT, 1, true) \
+        VK_SCAN_CASES_P4_S(Q, MT, 2, true)
+
+#define VK_SCAN_TABLE_P4(Q)                                                 \
+    template <>                                                             \
+    const void* scan_kernel_p4_for<Q>(int mt, int ilp, int s, bool prune) { \
+        switch ((prune ? 10000 : 0) + mt * 100 + ilp * 10 + s) {            \
+            VK_SCAN_CASES_P4_MT(Q, 16)                                      \
+            VK_SCAN_CASES_P4_MT(Q, 32)                                      \
+            VK_SCAN_CASES_P4_MT(Q, 64)                                      \
             default: return nullptr;                                        \
         }                                                                   \
     }

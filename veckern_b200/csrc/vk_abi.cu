@@ -173,6 +173,8 @@ int s_for_k(int k) { return k <= 32 ? 1 : k <= 64 ? 2 : 4; }
 struct vk_index {
     int device = 0;
     int m = 0, dsub = 0, W = 0;
+    int nbits = 8;  // bits per sub-code: 8 (256 centroids per sub-space) or 4 (16 centroids, two codes per byte)
+    int mb = 0;     // code bytes per row: m (8-bit) or ceil(m / 2) (4-bit)
     int64_t n = 0, n_pad = 0, id_base = 0;
     float* centroids = nullptr;
     uint4* codes = nullptr;
@@ -210,7 +212,7 @@ namespace {
 
 struct Plan {
     int Q = 1, ilp = 1, stages = kStagesMax, S = 1, mt = 0, merge_slots = 1;
-    bool prune = false, h16 = false, ivf = false;
+    bool prune = false, h16 = false, ivf = false, p4 = false;
     int threads = 0, blocks_per_sm = 0, grid = 0;
     int groups = 0, chunks = 0;
     int64_t chunk_len = 0, first_len = 0;
@@ -230,6 +232,9 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     p.prune = t.early_abandon != 0 && p.mt != 0;
     p.h16 = t.lut_precision == VK_LUT_F16;
     p.ivf = ivf;
+    p.p4 = ix->nbits == 4;
+    if (p.p4 && (p.h16 || ivf))
+        return fail(VK_ERR_UNSUPPORTED, "4-bit PQ indexes are searched with fp32 LUTs and without IVF lists");
     if (p.h16 && p.mt == 0)
         return fail(VK_ERR_UNSUPPORTED, "half-precision LUTs need m = 16, 32 or 64 (m = %d)", ix->m);
     if (ivf && (p.h16 || (ix->m != 16 && ix->m != 32)))
@@ -240,21 +245,23 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     Q = (int)std::min<int64_t>(Q, need);
     if (p.h16) Q = Q >= 8 ? 8 : 4;  // half LUT entries hold 4 or 8 queries
     if (ivf) Q = Q >= 8 ? 8 : 4;    // IVF items hold 4 or 8 queries
-    const int ilp_req = (p.prune || p.h16 || ivf) ? std::min(t.vectors_per_step, 2) : t.vectors_per_step;
+    if (p.p4) Q = Q >= 8 ? 8 : 4;   // 4-bit kernels are built for 4 or 8 queries
+    const int ilp_req =
+        (p.prune || p.h16 || ivf || p.p4) ? std::min(t.vectors_per_step, 2) : t.vectors_per_step;
     p.ilp = ilp_req;
     p.stages = kStagesMax;
     // warps per block as the kernel is instantiated (vk::scan_warps); the generic-m kernel uses its table size
-    auto warps = [&](int q) { return vk::scan_warps(q, p.mt, p.h16); };
+    auto warps = [&](int q) { return vk::scan_warps(q, p.mt, p.h16, p.p4); };
     auto slots = [&](int q) { return (uint32_t)q * warps(q) * k * 8u <= 16384u ? q : 1; };  // parallel merges
     auto fits = [&](int q, int ilp, int st) {
-        return vk::scan_smem_plan(q, ix->m, ix->W, ilp, warps(q), st, k, p.prune, slots(q), p.h16, p.ivf).total <=
+        return vk::scan_smem_plan(q, ix->m, ix->W, ilp, warps(q), st, k, p.prune, slots(q), p.h16, p.ivf, p.p4).total <=
                (uint32_t)ix->smem_optin;
     };
     for (;;) {
         if (fits(Q, p.ilp, p.stages)) break;
         if (p.stages > 2) { --p.stages; continue; }
         if (p.ilp > 1) { p.ilp /= 2; p.stages = kStagesMax; continue; }
-        if (Q > (p.h16 || p.ivf ? 4 : 1)) { Q /= 2; p.ilp = ilp_req; p.stages = kStagesMax; continue; }
+        if (Q > (p.h16 || p.ivf || p.p4 ? 4 : 1)) { Q /= 2; p.ilp = ilp_req; p.stages = kStagesMax; continue; }
         return fail(VK_ERR_INVALID, "LUT does not fit in shared memory (m = %d needs %u bytes, device allows %d)",
                     ix->m, vk::scan_smem_plan(p.h16 ? 4 : 1, ix->m, ix->W, 1, warps(p.h16 ? 4 : 1), 2, k, p.prune, 1,
                                               p.h16).total,
@@ -266,11 +273,15 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     if (ivf)
         p.fn = Q == 8 ? vk::scan_kernel_ivf_for<8>(p.mt, p.ilp, p.S, p.prune)
                       : vk::scan_kernel_ivf_for<4>(p.mt, p.ilp, p.S, p.prune);
+    else if (p.p4)
+        p.fn = Q == 8 ? vk::scan_kernel_p4_for<8>(p.mt, p.ilp, p.S, p.prune)
+                      : vk::scan_kernel_p4_for<4>(p.mt, p.ilp, p.S, p.prune);
     else
         p.fn = scan_kernel_ptr(Q, p.mt, p.ilp, p.S, p.prune, p.h16);
     if (!p.fn) return fail(VK_ERR_UNSUPPORTED, "no scan kernel for Q=%d m=%d ilp=%d", Q, ix->m, p.ilp);
     p.merge_slots = slots(Q);
-    p.smem = vk::scan_smem_plan(Q, ix->m, ix->W, p.ilp, nw, p.stages, k, p.prune, p.merge_slots, p.h16, p.ivf).total;
+    p.smem = vk::scan_smem_plan(Q, ix->m, ix->W, p.ilp, nw, p.stages, k, p.prune, p.merge_slots, p.h16, p.ivf, p.p4)
+                 .total;
     auto granted = ix->smem_granted.find(p.fn);
     if (granted == ix->smem_granted.end() || granted->second < p.smem) {
         VK_TRY_CUDA(cudaFuncSetAttribute(p.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
@@ -318,7 +329,7 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     if (t.blocks_per_query > 0) {
         chunks = std::min<int64_t>(t.blocks_per_query, max_chunks);
         // the pruned m = 16 scan addresses a chunk's rows in 24 bits of its queue entries
-        if (p.prune && vk::carry_queue(ix->m))
+        if (p.prune && vk::carry_queue(ix->m) && !p.p4)
             chunks = std::max<int64_t>(chunks, ceil_div(ix->n_pad, vk::CARRY_MAX_CHUNK_ROWS));
     } else {
         double best = 1e300;
@@ -395,7 +406,7 @@ struct WorkspaceBytes {
 };
 WorkspaceBytes workspace_bytes(const vk_index* ix, int64_t nq, int k, const Plan& p) {
     WorkspaceBytes b;
-    b.lut = (size_t)p.groups * p.Q * ix->m * vk::KSUB * (p.h16 ? 2 : 4);
+    b.lut = (size_t)p.groups * p.Q * ix->m * (p.p4 ? vk::KSUB4 : vk::KSUB) * (p.h16 ? 2 : 4);
     b.part = (size_t)nq * p.chunks * k * sizeof(int2);
     b.bound = (size_t)nq * sizeof(uint32_t);
     b.glist = (size_t)nq * k * sizeof(int2);
@@ -433,6 +444,16 @@ int launch_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const
             void* a1[] = {(void*)&cen,  (void*)&d_queries, (void*)&nq,    (void*)&m,     (void*)&dsub, (void*)&qmax,
                           (void*)&qexp, (void*)&lut,       (void*)&bound, (void*)&glist, (void*)&glock, (void*)&kk};
             VK_TRY_CUDA(cudaLaunchKernel(fh, dim3(ix->m, p.groups), dim3(vk::KSUB), a1, smem, st));
+        } else if (p.p4) {  // 16 sub-spaces x 16 centroids per block; the group's query sub-vectors in shared memory
+            const void* fn = p.Q == 8 ? reinterpret_cast<const void*>(&vk::lut4_kernel<8>)
+                                      : reinterpret_cast<const void*>(&vk::lut4_kernel<4>);
+            const size_t smem4 = (size_t)p.Q * 16 * ix->dsub * sizeof(float);
+            if (smem4 > 48 * 1024)
+                VK_TRY_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem4));
+            float* lutf = static_cast<float*>(lut);
+            void* args[] = {(void*)&cen, (void*)&d_queries, (void*)&nq, (void*)&m, (void*)&dsub, (void*)&lutf,
+                            (void*)&bound, (void*)&glist, (void*)&glock, (void*)&kk};
+            VK_TRY_CUDA(cudaLaunchKernel(fn, dim3((unsigned)ceil_div(ix->m, 16), p.groups), dim3(256), args, smem4, st));
         } else {
             const void* fn = lut_kernel_ptr(p.Q);
             if (smem > 48 * 1024)
@@ -598,7 +619,7 @@ int noalloc_scratch_address(int device, unsigned char** out) {
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 int create_common(int device, const float* centroids, int m, int dsub, int64_t n, int64_t id_base,
-                  vk_index** out, vk_index*& ix) {
+                  vk_index** out, vk_index*& ix, int nbits = 8) {
     if (!out) return fail(VK_ERR_INVALID, "out must not be NULL");
     *out = nullptr;
     if (!centroids) return fail(VK_ERR_INVALID, "centroids must not be NULL");
@@ -614,7 +635,9 @@ int create_common(int device, const float* centroids, int m, int dsub, int64_t n
     ix->device = device;
     ix->m = m;
     ix->dsub = dsub;
-    ix->W = (m + 15) / 16;
+    ix->nbits = nbits;
+    ix->mb = nbits == 4 ? (m + 1) / 2 : m;
+    ix->W = (ix->mb + 15) / 16;
     ix->n = n;
     ix->n_pad = ceil_div(n, 128) * 128;
     ix->id_base = id_base;
@@ -626,7 +649,7 @@ int create_common(int device, const float* centroids, int m, int dsub, int64_t n
     for (auto& e : ix->ev) VK_TRY_CUDA(cudaEventCreate(&e));
     VK_TRY_CUDA(cudaMalloc(&ix->flags, 4 * sizeof(int)));
     VK_TRY_CUDA(cudaMemsetAsync(ix->flags, 0, 4 * sizeof(int), ix->stream));
-    const size_t cbytes = (size_t)m * vk::KSUB * dsub * sizeof(float);
+    const size_t cbytes = (size_t)m * (nbits == 4 ? vk::KSUB4 : vk::KSUB) * dsub * sizeof(float);
     VK_TRY_CUDA(cudaMalloc(&ix->centroids, cbytes));
     VK_TRY_CUDA(cudaMemcpyAsync(ix->centroids, centroids, cbytes, cudaMemcpyHostToDevice, ix->stream));
     VK_TRY_CUDA(cudaMalloc(&ix->codes, (size_t)ix->n_pad * ix->W * sizeof(uint4)));
@@ -637,10 +660,18 @@ int create_common(int device, const float* centroids, int m, int dsub, int64_t n
     return VK_OK;
 }
 
+unsigned grid_for(int64_t total, int sm_count) {
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), (int64_t)sm_count * 16));
+}
+
 // Lane placement of the rows of every 64-row window (vk::place_rows_kernel), on the index stream after the codes
 // are in place. The objective follows the LUT layout the default plan picks for this m: 16-byte entries (Q >= 4)
 // up to m = 32, 8-byte entries (Q = 2) beyond; its weights follow the pruned scan's phase-A depths.
 cudaError_t place_rows(vk_index* ix) {
+    if (ix->nbits == 4) {  // 4-bit LUT fetches never conflict (one 128-byte table per query pair): rows stay in order
+        vk::identity_perm_kernel<<<grid_for(ix->n_pad, ix->sm_count), 256, 0, ix->stream>>>(ix->perm, ix->n_pad);
+        return cudaGetLastError();
+    }
     constexpr int kSteps = 4096;
     constexpr uint64_t kKey = 0x6c616e6570696b73ull;
     const int mt = (ix->m == 16 || ix->m == 32 || ix->m == 64) ? ix->m : 0;
@@ -655,10 +686,6 @@ cudaError_t place_rows(vk_index* ix) {
         vk::place_rows_kernel<16><<<grid, 128, smem, ix->stream>>>(ix->codes, ix->n, ix->n_pad, ix->m, ix->W,
                                                                     ix->perm, first, last, kSteps, kKey);
     return cudaGetLastError();
-}
-
-unsigned grid_for(int64_t total, int sm_count) {
-    return (unsigned)std::max<int64_t>(1, std::min<int64_t>(ceil_div(total, 256), (int64_t)sm_count * 16));
 }
 
 }  // namespace
@@ -708,24 +735,29 @@ int vk_device_info(int device, vk_device_info_t* out) {
     return VK_OK;
 }
 
-int vk_index_create(int device, const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
-                    int64_t id_base, vk_index_t** out) {
+}  // extern "C"
+
+namespace {
+// vk_index_create and vk_index_create_pq4: row-major codes (mb bytes per row) from HOST memory.
+int index_from_host(int device, const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
+                    int64_t id_base, int nbits, vk_index_t** out) {
     if (!codes) return fail(VK_ERR_INVALID, "codes must not be NULL");
     DeviceGuard guard(device);
     if (guard.err != cudaSuccess) return fail(VK_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(guard.err));
     vk_index* ix = nullptr;
-    int rc = create_common(device, centroids, m, dsub, n, id_base, out, ix);
+    int rc = create_common(device, centroids, m, dsub, n, id_base, out, ix, nbits);
     if (rc == VK_OK) {
         // Upload row-major codes in slices through one staging buffer and interleave each slice on the device.
+        const int mb = ix->mb;
         const int64_t slice = std::min<int64_t>(ceil_div(n, 32) * 32, int64_t(1) << 22);
         uint8_t* staging = nullptr;
-        cudaError_t e = cudaMalloc(&staging, (size_t)slice * m);
+        cudaError_t e = cudaMalloc(&staging, (size_t)slice * mb);
         for (int64_t r0 = 0; e == cudaSuccess && r0 < n; r0 += slice) {
             const int64_t cnt = std::min(slice, n - r0);
-            e = cudaMemcpyAsync(staging, codes + r0 * m, (size_t)cnt * m, cudaMemcpyHostToDevice, ix->stream);
+            e = cudaMemcpyAsync(staging, codes + r0 * mb, (size_t)cnt * mb, cudaMemcpyHostToDevice, ix->stream);
             if (e == cudaSuccess) {
                 vk::interleave_kernel<<<grid_for(ceil_div(cnt, 32) * 32 * ix->W, ix->sm_count), 256, 0, ix->stream>>>(
-                    staging, r0, cnt, n, m, ix->W, ix->codes);
+                    staging, r0, cnt, n, mb, ix->W, ix->codes);
                 e = cudaGetLastError();
             }
             if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);  // staging is reused
@@ -743,6 +775,28 @@ int vk_index_create(int device, const float* centroids, int m, int dsub, const u
         return rc;
     }
     *out = ix;
+    return VK_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int vk_index_create(int device, const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
+                    int64_t id_base, vk_index_t** out) {
+    return index_from_host(device, centroids, m, dsub, codes, n, id_base, 8, out);
+}
+
+int vk_index_create_pq4(int device, const float* centroids, int m, int dsub, const uint8_t* codes, int64_t n,
+                        int64_t id_base, vk_index_t** out) {
+    if (out) *out = nullptr;
+    if (m != 16 && m != 32 && m != 64)
+        return fail(VK_ERR_UNSUPPORTED, "4-bit PQ indexes support m = 16, 32 or 64 (m = %d)", m);
+    return index_from_host(device, centroids, m, dsub, codes, n, id_base, 4, out);
+}
+
+int vk_index_bits(const vk_index_t* ix, int* nbits) {
+    if (!ix || !nbits) return fail(VK_ERR_INVALID, "index and nbits must not be NULL");
+    *nbits = ix->nbits;
     return VK_OK;
 }
 
@@ -822,11 +876,11 @@ int vk_index_get_codes(const vk_index_t* ix, int64_t first, int64_t count, uint8
     if (count == 0) return VK_OK;
     DeviceGuard guard(ix->device);
     uint8_t* d = nullptr;
-    VK_TRY_CUDA(cudaMalloc(&d, (size_t)count * ix->m));
-    vk::deinterleave_kernel<<<grid_for((count + 2 * vk::PLACE_WINDOW) * ix->m, ix->sm_count), 256, 0, ix->stream>>>(
-        ix->codes, ix->perm, first, count, ix->m, ix->W, d);
+    VK_TRY_CUDA(cudaMalloc(&d, (size_t)count * ix->mb));
+    vk::deinterleave_kernel<<<grid_for((count + 2 * vk::PLACE_WINDOW) * ix->mb, ix->sm_count), 256, 0, ix->stream>>>(
+        ix->codes, ix->perm, first, count, ix->mb, ix->W, d);
     cudaError_t e = cudaGetLastError();
-    if (e == cudaSuccess) e = cudaMemcpyAsync(out, d, (size_t)count * ix->m, cudaMemcpyDeviceToHost, ix->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, d, (size_t)count * ix->mb, cudaMemcpyDeviceToHost, ix->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ix->stream);
     cudaFree(d);
     if (e != cudaSuccess) return fail(VK_ERR_CUDA, "reading codes failed: %s", cudaGetErrorString(e));
@@ -835,6 +889,7 @@ int vk_index_get_codes(const vk_index_t* ix, int64_t first, int64_t count, uint8
 
 int vk_index_save(const vk_index_t* ix, const char* path) {
     if (!ix || !path) return fail(VK_ERR_INVALID, "index and path must not be NULL");
+    if (ix->nbits != 8) return fail(VK_ERR_UNSUPPORTED, "index files hold 8-bit codes only");
     DeviceGuard guard(ix->device);
     std::vector<float> cent((size_t)ix->m * vk::KSUB * ix->dsub);
     VK_TRY_CUDA(cudaMemcpy(cent.data(), ix->centroids, cent.size() * sizeof(float), cudaMemcpyDeviceToHost));
@@ -1382,6 +1437,7 @@ int vk_index_sync(vk_index_t* ix, void* stream) {
 int vk_distances(vk_index_t* ix, const float* queries, int64_t nq, int variant, const vk_tuning_t* tuning,
                  float* out, vk_timings_t* timings) {
     if (!ix) return fail(VK_ERR_INVALID, "index must not be NULL");
+    if (ix->nbits != 8) return fail(VK_ERR_UNSUPPORTED, "distances() is implemented for 8-bit indexes only");
     if (variant < 0 || variant > 8) return fail(VK_ERR_INVALID, "unknown scan variant %d", variant);
     if (is_fused_variant(variant)) return fail(VK_ERR_INVALID, "fused variants do not materialise distances");
     VK_TRY(check_variant(ix, variant));
@@ -1441,6 +1497,7 @@ int vk_distances(vk_index_t* ix, const float* queries, int64_t nq, int variant, 
 
 int vk_compute_lut_device(vk_index_t* ix, const float* d_queries, int64_t nq, float* d_lut, void* stream) {
     if (!ix) return fail(VK_ERR_INVALID, "index must not be NULL");
+    if (ix->nbits != 8) return fail(VK_ERR_UNSUPPORTED, "vk_compute_lut_device is implemented for 8-bit indexes only");
     if (nq < 0) return fail(VK_ERR_INVALID, "nq must be >= 0");
     if (nq == 0) return VK_OK;
     if (!d_queries || !d_lut) return fail(VK_ERR_INVALID, "queries and lut must not be NULL");

@@ -101,6 +101,41 @@ struct WarpTopK {
         }
     }
 
+    // N candidates per lane (x[u], xi[u], valid[u]), e.g. the rows of N 32-row groups: one ballot per group, then
+    // the admitted candidates inserted one at a time from one loop. Equivalent to N offer() calls (the k smallest of
+    // distinct (dist, id) pairs do not depend on the order they arrive in), with one copy of the insertion code
+    // instead of N where it is inlined.
+    template <int N>
+    __device__ __forceinline__ void offer_n(const float (&x)[N], const int32_t (&xi)[N], const bool (&valid)[N],
+                                            int k) {
+        unsigned mask[N];
+        static_for<N>([&](auto u) { mask[u] = __ballot_sync(FULL, valid[u] && admits(x[u], xi[u])); });
+        for (;;) {
+            int uu = -1;
+            unsigned mm = 0u;
+            static_for<N>([&](auto c) {
+                if (uu < 0 && mask[c] != 0u) {
+                    uu = c;
+                    mm = mask[c];
+                }
+            });
+            if (uu < 0) break;  // warp-uniform: the masks come from ballots
+            const int src = __ffs(mm) - 1;
+            float v = x[0];
+            int32_t vi = xi[0];
+            static_for<N>([&](auto c) {
+                if (c == uu) {
+                    mask[c] &= mask[c] - 1u;
+                    v = x[c];
+                    vi = xi[c];
+                }
+            });
+            const float cx = __shfl_sync(FULL, v, src);
+            const int32_t ci = __shfl_sync(FULL, vi, src);
+            if (admits(cx, ci)) insert(cx, ci, k);  // the threshold may have dropped since the ballot
+        }
+    }
+
     // Writes entries 0 .. k-1 (ascending) as (dist, id) pairs.
     __device__ __forceinline__ void store(int2* out, int k) const {
         const int lane = threadIdx.x & (WARP - 1);

@@ -34,6 +34,26 @@ def pq_encode(centroids: np.ndarray, x: np.ndarray) -> np.ndarray:
     return codes
 
 
+def pq4_train(x: np.ndarray, m: int, iters: int, seed: int = 1) -> np.ndarray:
+    """4-bit PQ codebooks: the same trainer with 16 centroids per sub-space -> [m, 16, d/m]."""
+    x = np.ascontiguousarray(x, np.float32)
+    n, d = x.shape
+    cent = np.empty((m, 16, d // m), np.float32)
+    _ok(host().vk_host_pq4_train(ptr(x), n, d, m, iters, seed, ptr(cent)), "pq4_train")
+    return cent
+
+
+def pq4_encode(centroids: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """First nearest of the 16 centroids per sub-space, packed two per byte (sub-code s in nibble s % 2, low
+    first, of byte s / 2) -> [n, ceil(m / 2)] uint8."""
+    centroids = np.ascontiguousarray(centroids, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    m, _, dsub = centroids.shape
+    codes = np.empty((x.shape[0], (m + 1) // 2), np.uint8)
+    _ok(host().vk_host_pq4_encode(ptr(centroids), m * dsub, m, ptr(x), x.shape[0], ptr(codes)), "pq4_encode")
+    return codes
+
+
 def pq_decode(centroids: np.ndarray, codes: np.ndarray) -> np.ndarray:
     centroids = np.ascontiguousarray(centroids, np.float32)
     codes = np.ascontiguousarray(codes, np.uint8)

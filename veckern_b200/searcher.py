@@ -3,6 +3,7 @@ C ABI: same names, argument meaning and errors (VkError, a RuntimeError, where t
 std::runtime_error).
 
     searcher = PQSearcher(centroids, codes)                   # centroids [m, 256, dsub] f32, codes [n, m] u8
+    searcher = PQSearcher(centroids4, codes4)                 # 4-bit PQ: [m, 16, dsub] f32, codes [n, m / 2] u8
     timings = searcher.search(queries, k, ScanVariant.FusedWarp, out)   # out: [nq, k] NEIGHBOR_DTYPE
     dist, ids = neighbors_split(out)
 """
@@ -118,10 +119,16 @@ class PQSearcher:
             self._h = _handle
         else:
             centroids = np.ascontiguousarray(centroids, np.float32)
-            if centroids.ndim != 3 or centroids.shape[1] != 256:
-                raise ValueError("centroids must be [m, 256, dsub] float32")
-            m, _, dsub = centroids.shape
-            if hasattr(codes, "data_ptr"):  # torch tensor already on the device
+            if centroids.ndim != 3 or centroids.shape[1] not in (16, 256):
+                raise ValueError("centroids must be [m, 256, dsub] (8-bit codes) or [m, 16, dsub] (4-bit codes) float32")
+            m, ksub, dsub = centroids.shape
+            if ksub == 16:  # 4-bit PQ: codes [n, m / 2], sub-code s in nibble s % 2 (low first) of byte s / 2
+                codes = np.ascontiguousarray(codes, np.uint8)
+                if codes.ndim != 2 or codes.shape[1] != (m + 1) // 2:
+                    raise ValueError("4-bit codes must be [n, ceil(m / 2)] uint8 (two sub-codes per byte)")
+                check(lib().vk_index_create_pq4(device, ptr(centroids), m, dsub, ptr(codes), codes.shape[0], id_base,
+                                                C.byref(self._h)), "vk_index_create_pq4")
+            elif hasattr(codes, "data_ptr"):  # torch tensor already on the device
                 n = codes.shape[0]
                 check(lib().vk_index_create_from_device(device, ptr(centroids), m, dsub, ptr(codes), n, id_base,
                                                         C.byref(self._h)), "vk_index_create_from_device")
@@ -135,6 +142,9 @@ class PQSearcher:
         check(lib().vk_index_info(self._h, C.byref(n), C.byref(m), C.byref(dsub), C.byref(base), C.byref(dev)))
         self.n, self.m, self.dsub, self.id_base, self.device = n.value, m.value, dsub.value, base.value, dev.value
         self.d = self.m * self.dsub
+        bits = C.c_int()
+        check(lib().vk_index_bits(self._h, C.byref(bits)))
+        self.nbits = bits.value  # 8, or 4 for 4-bit PQ
 
     @classmethod
     def generated(cls, centroids, seed: int, cdf: np.ndarray, row_first: int, n: int, *, device: int = 0,
