@@ -784,11 +784,23 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16, P4>()) sc
 #pragma unroll
                     for (int q = 0; q < Q; ++q) any |= valid[u] && top[q].admits(acc[u][q], ids[u]);
                 }
-                if (__any_sync(FULL, any)) {  // (one offer per row group: measured 4 % faster here than offer_n)
+                if (__any_sync(FULL, any)) {
+                    // 8-bit codes: one offer per row group (4 % faster here than offer_n at config 1); 4-bit codes:
+                    // offer_n (8 % faster for them)
+                    if constexpr (P4) {
+                        static_for<Q>([&](auto qc) {
+                            constexpr int q = decltype(qc)::value;
+                            float x[ILP];
 #pragma unroll
-                    for (int u = 0; u < ILP; ++u)
+                            for (int u = 0; u < ILP; ++u) x[u] = acc[u][q];
+                            top[q].offer_n(x, ids, valid, a.k);
+                        });
+                    } else {
 #pragma unroll
-                        for (int q = 0; q < Q; ++q) top[q].offer(acc[u][q], ids[u], valid[u], a.k);
+                        for (int u = 0; u < ILP; ++u)
+#pragma unroll
+                            for (int q = 0; q < Q; ++q) top[q].offer(acc[u][q], ids[u], valid[u], a.k);
+                    }
                 }
             } else {
                 // The query group's global bounds, loaded now (lane q: query q) so that the L2 latency hides
@@ -963,20 +975,23 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16, P4>()) sc
                 // ---- phase B: finish the queued pairs 32 at a time from sub-space D = dep, two sub-spaces per step,
                 // each lane dropping out as soon as its sum exceeds its query's bound. One copy per depth, so that
                 // every sub-space index stays a compile-time constant.
-                auto phase_b = [&](auto dc) {
-                    constexpr int D = decltype(dc)::value;
-                    for (int base = 0; base < cnt; base += 32) {
-                        const int e = base + lane;
-                        bool live = e < cnt;
-                        const int2 ent = live ? my_queue[e] : make_int2(0, 0);
-                        float x = __int_as_float(ent.x);
-                        const int r = ent.y & 0xffff, q = ent.y >> 16;
-                        float bq = bnd[0];
+                // One copy of the batch loop and its Q top-k offers; only the lookups are specialised per depth D
+                // (every sub-space index a compile-time constant).
+                for (int base = 0; base < cnt; base += 32) {
+                    const int e = base + lane;
+                    bool live = e < cnt;
+                    const int2 ent = live ? my_queue[e] : make_int2(0, 0);
+                    float x = __int_as_float(ent.x);
+                    const int r = ent.y & 0xffff, q = ent.y >> 16;
+                    float bq = bnd[0];
 #pragma unroll
-                        for (int qq = 1; qq < Q; ++qq)
-                            if (q == qq) bq = bnd[qq];
-                        const unsigned char* lq = lut_smem + lut_query_base<Q, H16, P4>(q, MT);
-                        const uint4* rowp = st + (r >> 5) * W_T * 32 + (r & 31);
+                    for (int qq = 1; qq < Q; ++qq)
+                        if (q == qq) bq = bnd[qq];
+                    const unsigned char* lq = lut_smem + lut_query_base<Q, H16, P4>(q, MT);
+                    const uint4* rowp = st + (r >> 5) * W_T * 32 + (r & 31);
+                    static_for<(SAX - SA) / 2 + 1>([&](auto dc) {
+                        constexpr int D = SA + 2 * decltype(dc)::value;
+                        if (dep != D) return;
                         uint4 cw = make_uint4(0, 0, 0, 0);
 #pragma unroll
                         for (int s = D; s < MT; s += 2) {
@@ -997,23 +1012,17 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16, P4>()) sc
                                 live = live && !(x > bq);
                             }
                         }
-                        const int32_t id = row_id(r);
-                        if (__any_sync(FULL, live)) {  // usually every pair of the batch was abandoned
+                    });
+                    const int32_t id = row_id(r);
+                    if (__any_sync(FULL, live)) {  // usually every pair of the batch was abandoned
 #pragma unroll
-                            for (int qq = 0; qq < Q; ++qq) {
-                                if (__any_sync(FULL, live && q == qq)) {
-                                    top[qq].offer(x, id, live && q == qq, a.k);
-                                    bnd[qq] = fminf(bnd[qq], top[qq].thr_d);
-                                }
+                        for (int qq = 0; qq < Q; ++qq) {
+                            if (__any_sync(FULL, live && q == qq)) {
+                                top[qq].offer(x, id, live && q == qq, a.k);
+                                bnd[qq] = fminf(bnd[qq], top[qq].thr_d);
                             }
                         }
                     }
-                };
-                if (cnt > 0) {
-                    static_for<(SAX - SA) / 2 + 1>([&](auto e) {
-                        constexpr int D = SA + 2 * decltype(e)::value;
-                        if (dep == D) phase_b(Int<D>{});
-                    });
                 }
                 __syncwarp();  // the queue and the stage slot are free again
                 if (lane == 0) refill();
