@@ -358,7 +358,8 @@ __host__ __device__ inline ScanSmem scan_smem_plan(int Q, int m, int W, int ilp,
 // its window; ids, and so results, are those of the rows.
 constexpr int PLACE_WINDOW = 64;
 
-// 4-bit codes (p4) carry half the bits per sub-space: their first vote comes after half of the sub-spaces.
+// 4-bit codes (p4) carry half the bits per sub-space: their first vote comes after half of the sub-spaces (at config 1
+// with m = 32, first votes after 12 / 16 / 20 sub-spaces measured 4.18 / 3.36 / 3.50 ms).
 __host__ __device__ constexpr int prune_first(int m, bool p4 = false) {
     return p4 ? m / 2 : m <= 16 ? 8 : m <= 32 ? 12 : 24;
 }
