@@ -172,6 +172,18 @@ def test_random_shapes_against_oracle(port, n, m, dsub, nq, k):
             assert_same_topk(d, i, ed, ei, f"n={n} m={m} Q={tq}")
 
 
+@pytest.mark.parametrize("prune", [True, False])
+def test_windowed_item_order_many_query_groups(port, prune):
+    """Many query groups (1,400 queries of m = 64: 700 groups x 128 KB of LUTs, more than the L2 share for one
+    window) run window by window of groups; results stay those of the oracle."""
+    cent, codes, q = random_db(41, 200_003, 64, 2, 1_400)
+    ed, ei = port.adc_search(cent, codes, q, 10)
+    d, i, shape = gpu_search(cent, codes, q, 10, tuning=Tuning(queries_per_block=2, vectors_per_step=2,
+                                                              early_abandon=prune))
+    assert shape.grid_y == 700
+    assert_same_topk(d, i, ed, ei, f"windowed order prune={prune}")
+
+
 def test_rejections(golden):
     g = golden("gpu_fixture")
     with PQSearcher(g["centroids"], g["codes"]) as s:

@@ -265,6 +265,8 @@ struct ScanArgs {
                          // first_len + (c - 1) * chunk_len
     int64_t id_base;     // global id = id_base + row
     int m, W, nq, groups, chunks, k, stages;
+    int group_window;       // flat search: items run window by window of this many query groups, chunk-major inside
+                            // a window, so that the window's LUTs and the current chunk's codes stay in L2 together
     int merge_slots;        // 1 or Q (see scan_smem_plan)
     long long wait_budget;  // SM cycles a bounded wait may take
     // Cooperative sharded search (pruned scan): xb = this shard's exchange array, xpeer = the other shards'
@@ -566,7 +568,14 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16, P4>()) sc
         const int item = *s_item;
         if (item >= items || *s_abort) break;
         // flat: (chunk, query group); IVF: the item's list, and its own LUT (g = item)
-        const int chunk = IVF ? 0 : item / a.groups, g = IVF ? item : item - chunk * a.groups;
+        int chunk = 0, g = item;
+        if constexpr (!IVF) {  // window of group_window groups, then chunk, then group (group_window = groups: chunk-major)
+            const int per_win = a.group_window * a.chunks;
+            const int win = item / per_win, r = item - win * per_win;
+            const int g0 = win * a.group_window, gw = min(a.group_window, a.groups - g0);
+            chunk = r / gw;
+            g = g0 + (r - chunk * gw);
+        }
         const int list = IVF ? a.ivf_item_list[item] : 0;
         // global index of the item's query q (-1: padding); IVF: the probe slot its list is for that query
         auto qidx = [&](int q) -> int64_t {

@@ -94,6 +94,7 @@ struct DevBuf {
     }
 };
 
+constexpr size_t kL2WindowBytes = size_t(80) << 20;  // L2 share for one window's LUTs plus two chunks' codes
 constexpr int64_t kMaxRowsPerChunk = 1 << 20;       // L2 locality: a chunk's codes stay well inside the 126 MB L2
 constexpr size_t kLutBudgetBytes = size_t(1) << 30;  // LUT buffer cap per query batch
 constexpr size_t kDistanceBudgetBytes = size_t(512) << 20;  // distances(): the reference's 512 MB cap
@@ -211,7 +212,7 @@ struct vk_index {
 namespace {
 
 struct Plan {
-    int Q = 1, ilp = 1, stages = kStagesMax, S = 1, mt = 0, merge_slots = 1;
+    int Q = 1, ilp = 1, stages = kStagesMax, S = 1, mt = 0, merge_slots = 1, group_window = 1;
     bool prune = false, h16 = false, ivf = false, p4 = false;
     int threads = 0, blocks_per_sm = 0, grid = 0;
     int groups = 0, chunks = 0;
@@ -350,6 +351,17 @@ int plan_scan(const vk_index* ix, int64_t nq, int k, const vk_tuning_t& t, Plan&
     if (p.prune && t.blocks_per_query <= 0)
         p.first_len = std::max<int64_t>(tile_rows, p.chunk_len / 2 / tile_rows * tile_rows);
     p.chunks = (int)(1 + ceil_div(std::max<int64_t>(0, ix->n_pad - p.first_len), p.chunk_len));
+    // Item order: chunk-major over all query groups while their LUTs and two chunks of codes fit in the L2 share;
+    // otherwise window by window of as many groups as fit (each chunk's codes then come from HBM once per window
+    // instead of once per group whose LUT was evicted).
+    {
+        const size_t lut_group = (size_t)p.Q * ix->m * (p.p4 ? vk::KSUB4 : vk::KSUB) * (p.h16 ? 2 : 4);
+        const size_t chunk_bytes = (size_t)p.chunk_len * ((size_t)ix->W * 16 + 1);
+        const size_t room = kL2WindowBytes > 2 * chunk_bytes ? kL2WindowBytes - 2 * chunk_bytes : 0;
+        p.group_window = (size_t)p.groups * lut_group <= room
+                             ? p.groups
+                             : (int)std::max<size_t>(1, std::min<size_t>(room / lut_group, (size_t)p.groups));
+    }
     const int64_t items = (int64_t)p.groups * p.chunks;
     if (items > std::numeric_limits<int>::max() / 2)
         return fail(VK_ERR_UNSUPPORTED, "too many work items (%lld); search fewer queries per call", (long long)items);
@@ -487,6 +499,7 @@ int launch_search(vk_index* ix, const float* d_queries, int64_t nq, int k, const
         a.nq = (int)nq;
         a.groups = p.groups;
         a.chunks = p.chunks;
+        a.group_window = p.group_window;
         a.k = k;
         a.stages = p.stages;
         a.merge_slots = p.merge_slots;
@@ -1865,6 +1878,7 @@ int ivf_run(vk_ivf* ivf, const float* d_queries, int64_t nq, int k, int nprobe, 
         a.W = ix->W;
         a.nq = (int)nq;
         a.groups = 1;
+        a.group_window = 1;
         a.chunks = 1;
         a.k = k;
         a.stages = p.stages;
