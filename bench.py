@@ -181,8 +181,8 @@ class ClockSampler:
 NCU_TRAFFIC = {
     ("c1", 1_000_000, 16, 1000, 10): {"dram_bytes_per_launch": 33_659_136, "kernel": "scan_kernel<8,16,2,1,16,1>"},
     ("c3", 10_000_000, 16, 1000, 10): {"dram_bytes_per_launch": 196_180_000, "kernel": "scan_kernel<8,16,2,1,16,1>"},
-    # ncu prints this capture in GB with two decimals
-    ("c3", 100_000_000, 16, 10_000, 10): {"dram_bytes_per_launch": 18_047_000_000, "kernel": "scan_kernel<8,16,2,1,16,1>"},
+    # ncu prints this capture in GB / MB with two decimals (windowed item order: 16.75 GB read + 188.51 MB written)
+    ("c3", 100_000_000, 16, 10_000, 10): {"dram_bytes_per_launch": 16_938_510_000, "kernel": "scan_kernel<8,16,2,1,16,1>"},
 }
 
 
