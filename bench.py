@@ -903,6 +903,8 @@ def run_ours(args):
         lookups = float(nq) * (hi - lo) * m  # per rank (rank 0's shard) per launch
         achieved = lookups / (scan_mean / 1e3)
         smem_peak_bytes = 128.0 * info.sm_count * sm_mhz * 1e6
+        if world > 1:  # the shard searches above ran on the device path: one untimed host call records the plan
+            s.search(np.ascontiguousarray(w.queries), k)
         Q = s.last_launch().queries_per_block
         sample = 1 << 17
         if w.codes is not None:
