@@ -175,7 +175,7 @@ class ClockSampler:
 
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the default scan kernel, from ncu
-# captures of these workloads on one B200 (the capture commands and their other counters are in profiles/). Keyed by
+# captures of these workloads on one B200 (1-pass dram and duration metrics of the scan kernel). Keyed by
 # (config, rows scanned per GPU, m, nq, k); a run whose shard matches no capture reports the bytes scaled from the
 # capture of the same config by rows (codes and placement bytes grow with rows, LUT bytes with nq), marked scaled.
 NCU_TRAFFIC = {

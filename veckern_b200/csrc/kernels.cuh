@@ -815,14 +815,12 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16, P4>()) sc
             } else {
                 // The query group's global bounds, loaded now (lane q: query q) so that the L2 latency hides
                 // behind phase A; other warps and blocks keep lowering them.
+                // (the other shards' bounds of a cooperative search are read at item start only, and this shard's
+                // lowered bounds are offered to them at item end: no per-tile cost)
                 uint32_t gbits = 0x7f800000u;
-                unsigned long long gx = 0ull;
                 if (lane < Q) {
                     const int64_t qi = qidx(lane);
-                    if (qi >= 0) {
-                        gbits = __ldcg(a.bound + qi);
-                        gx = coop_load(a, qi);
-                    }
+                    if (qi >= 0) gbits = __ldcg(a.bound + qi);
                 }
                 // ---- phase A: sub-spaces [0, SA) of every row, all Q queries per fetch
                 float acc[ILP][Q];
@@ -844,7 +842,7 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16, P4>()) sc
                     }
                 };
                 static_for<SA>(phase_a);
-                const float gb = __uint_as_float(min(gbits, coop_decode(a, gx)));  // the loads have landed by now
+                const float gb = __uint_as_float(gbits);  // the load has landed by now
                 float bnd[Q];
 #pragma unroll
                 for (int q = 0; q < Q; ++q) {
@@ -1044,7 +1042,6 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16, P4>()) sc
                         if (lane == 0) {
                             const int64_t qi = qidx(q);
                             atomicMin(a.bound + qi, __float_as_uint(top[q].thr_d));
-                            coop_publish(a, qi, __float_as_uint(top[q].thr_d));
                         }
                         known[q] = top[q].thr_d;
                     }
