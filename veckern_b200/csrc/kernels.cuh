@@ -1101,10 +1101,16 @@ __global__ void __launch_bounds__(NW * 32, scan_min_blocks<Q, MT, H16, P4>()) sc
                     __syncwarp();
                     if (lane == 0) atomicExch(a.glock + qi, 0);
                 }
-                if (lane == 0 && mt.thr_i != SENTINEL_ID && mt.thr_d < kb)
-                {
-                    atomicMin(a.bound + qi, __float_as_uint(mt.thr_d));
-                    coop_publish(a, qi, __float_as_uint(mt.thr_d));
+                if (lane == 0) {
+                    const bool lower = mt.thr_i != SENTINEL_ID && mt.thr_d < kb;
+                    if (lower) atomicMin(a.bound + qi, __float_as_uint(mt.thr_d));
+                    // Cooperative search: offer the other shards this shard's bound of the query as it stands now
+                    // (the warps lowered it per tile too), once per item.
+                    if (a.npeers > 0) {
+                        uint32_t b = __ldcg(a.bound + qi);
+                        if (lower) b = min(b, __float_as_uint(mt.thr_d));
+                        if (b != 0x7f800000u) coop_publish(a, qi, b);
+                    }
                 }
             }
         };
